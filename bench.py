@@ -1,0 +1,391 @@
+#!/usr/bin/env python
+"""Benchmark of the batched 142-feature extraction on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One process per GPU (torchrun for N > 1).  A step is one pass of the feature
+path over one batch: 65,536 aircraft per GPU (at N = 8 the
+whole job is config 3's 524,288), seeded synthetic inputs generated on the
+host.  Rank 0 prints one JSON line:
+
+  value      samples/s over all ranks, inputs resident in HBM, timed with CUDA
+             events on the launching stream, max over ranks
+  e2e        the same metric through the reference-facing host ABI
+             tb_cuda_extract_features_host (page-locked host buffers; the
+             host->device input copy and device->host feature copy are inside
+             every step)
+  roofline   achieved HBM GB/s of the kernel (algorithmic bytes / average
+             launch time) against the measured copy bandwidth
+  cpu_baseline  the reference's own CPU feature code (oracle/_ref) on this
+             host's cores, a bounded sample of the same workload (rank 0, N=1)
+
+--impl reference times that reference CPU code alone on all host cores (rank
+0 only; other ranks exit at once).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import turbinator_c_b200 as tb  # noqa: E402
+from turbinator_c_b200.shard import shard_range  # noqa: E402
+
+METRIC = "sensor-feature samples/sec"
+UNIT = "samples/s"
+BATCH_PER_GPU = 65536
+SEED = 2
+FALLBACK_HBM_GBS = 6650.0
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "features_staged_kernel_traffic.txt")
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--batch", type=int, default=BATCH_PER_GPU, help="aircraft per GPU")
+    p.add_argument("--e2e-steps", type=int, default=0, help="host-ABI steps (default: --steps, max 20)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=4.0, help="target wall time of the CPU sample")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------- helpers
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def measured_hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic_per_sample():
+    """DRAM bytes per aircraft of the staged kernel from the committed ncu summary."""
+    try:
+        with open(PROFILE_SUMMARY) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_sample:"):
+                    return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons of one GPU through NVML while
+    active() is true (only samples taken inside timed regions are kept)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons = [], 0
+        self.max_mhz = None
+        self._on = threading.Event()
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            if visible:
+                ids = [v.strip() for v in visible.split(",") if v.strip()]
+                idx = int(ids[device_index]) if ids[device_index].isdigit() else device_index
+            else:
+                idx = device_index
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._nvml = pynvml
+            self.ok = True
+        except Exception:  # NVML unavailable: report no clocks rather than guess
+            return
+        self._t = threading.Thread(target=self._run, args=(period_s,), daemon=True)
+        self._t.start()
+
+    def _run(self, period):
+        nv = self._nvml
+        while not self._stop.is_set():
+            if self._on.is_set():
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                    try:
+                        r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                    except AttributeError:
+                        r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                    self.samples.append(mhz)
+                    self.reasons |= int(r)
+                except Exception:
+                    pass
+            time.sleep(period)
+
+    def active(self, on: bool):
+        (self._on.set if on else self._on.clear)()
+
+    def close(self):
+        self._stop.set()
+
+    def summary(self):
+        if not self.ok:
+            return None
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples),
+                "source": "nvml"}
+
+
+def cpu_description():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def time_reference_cpu(obs, mission, cams, target_s: float):
+    """Times the reference's tb_train_extract_features_cpu (oracle/_ref, or the
+    restated oracle when the reference build is absent) on all host threads
+    over a bounded leading sample of the batch.  Returns a dict."""
+    import oracle  # test infrastructure: the CPU baseline only
+
+    kind = "reference" if oracle.have_reference() else "port"
+    timed = oracle.timed_reference if kind == "reference" else oracle.timed_port
+    threads = host_threads()
+    n = obs.shape[0]
+    probe = min(n, max(threads * 64, 2048))
+    out = np.empty((n, 142), np.float32)
+    t = timed(obs[:probe], mission[:probe], cams[:probe], out[:probe], threads)
+    rate = probe / max(t, 1e-9)
+    sample = int(min(n, max(probe, rate * target_s)))
+    t = timed(obs[:sample], mission[:sample], cams[:sample], out[:sample], threads)
+    return {"value": sample / t, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"first {sample} of the {n}-aircraft batch, {threads} threads over contiguous "
+                      f"ranges, {t:.2f} s wall; host CPU: {cpu_description()}"}
+
+
+# ---------------------------------------------------------------- arms
+
+def run_reference_arm(args, rank: int, world: int):
+    if rank != 0:
+        return
+    import oracle  # test infrastructure: the reference arm times the reference CPU code
+
+    obs, mission, cams, _ = tb.generate(SEED, 0, args.batch, total=args.batch * world,
+                                        threads=host_threads())
+    kind = "reference" if oracle.have_reference() else "port"
+    timed = oracle.timed_reference if kind == "reference" else oracle.timed_port
+    threads = host_threads()
+    out = np.empty((args.batch, 142), np.float32)
+    probe = min(args.batch, max(threads * 64, 2048))
+    rate = probe / max(timed(obs[:probe], mission[:probe], cams[:probe], out[:probe], threads), 1e-9)
+    # each step: the whole batch if it takes <= ~3 s, else a leading sample of it
+    per_step = int(min(args.batch, max(probe, rate * 3.0)))
+    for _ in range(args.warmup):
+        timed(obs[:per_step], mission[:per_step], cams[:per_step], out[:per_step], threads)
+    total_t = 0.0
+    for _ in range(args.steps):
+        total_t += timed(obs[:per_step], mission[:per_step], cams[:per_step], out[:per_step], threads)
+    value = per_step * args.steps / total_t
+    sample = (f"{per_step} of the {args.batch}-aircraft batch per step, {threads} threads; "
+              f"host CPU: {cpu_description()}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total_t / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded SplitMix64 generator, BASELINE value model)",
+        "config": workload_config(args, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args, world):
+    return {
+        "workload": f"config2-per-GPU: {args.batch} aircraft per GPU (seed {SEED}); "
+                    f"{world} GPU(s) -> {args.batch * world} aircraft"
+                    + (" (= config 3)" if args.batch * world == 524288 else ""),
+        "batch_per_gpu": args.batch,
+        "global_batch": args.batch * world,
+        "abi": "u8 cameras (reference cuda_features.h)",
+        "bytes_per_sample": tb.BYTES_PER_SAMPLE,
+        "parallelism": f"sample-sharded x{world}, no collective on the data path",
+        "l2": f"inputs {args.batch * tb.BYTES_PER_SAMPLE / 1e9:.2f} GB per GPU > 126 MB L2; no flush needed",
+    }
+
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    tb.load_library()
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    gen_threads = max(1, host_threads() // max(local_world, 1))
+
+    total = args.batch * world
+    first, count = shard_range(total, rank, world)
+    obs, mission, cams, _ = tb.generate(SEED, first, count, total=total, threads=gen_threads, pinned=True)
+    d_obs = torch.from_numpy(obs).to(dev)
+    d_mis = torch.from_numpy(mission).to(dev)
+    d_cam = torch.from_numpy(cams).to(dev)
+    d_out = torch.empty((count, 142), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(local_rank)
+
+    # ---- value: kernel only, inputs resident in HBM
+    for _ in range(max(args.warmup, 3)):
+        assert tb.tb_cuda_extract_features_device(d_obs, d_mis, d_cam, d_out, count, stream) == 1
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.active(True)
+    start.record(stream)
+    for _ in range(args.steps):
+        tb.tb_cuda_extract_features_device(d_obs, d_mis, d_cam, d_out, count, stream)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks.active(False)
+    if tb.tb_cuda_synchronize(stream.cuda_stream) != 1:
+        raise RuntimeError("feature kernel reported a pipeline timeout during the timed region")
+    barrier()
+    kernel_s = start.elapsed_time(end) / 1e3
+    kernel_s_max = max_over_ranks(kernel_s)
+    value = total * args.steps / kernel_s_max
+
+    # ---- e2e: the reference-facing host ABI on page-locked host buffers
+    e2e_steps = args.e2e_steps or min(args.steps, 20)
+    out_host = torch.empty((count, 142), dtype=torch.float32, pin_memory=True).numpy()
+    fb = tb.FeatureBatch(local_rank, count)
+    for _ in range(max(1, min(args.warmup, 3))):
+        if fb.extract(obs, mission, cams, count, out_host) != 1:
+            raise RuntimeError(f"host ABI failed: {fb.error()}")
+    barrier()
+    clocks.active(True)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        if fb.extract(obs, mission, cams, count, out_host) != 1:
+            raise RuntimeError(f"host ABI failed: {fb.error()}")
+    e2e_s = time.perf_counter() - t0
+    clocks.active(False)
+    fb.close()
+    e2e_s_max = max_over_ranks(e2e_s)
+    e2e_value = total * e2e_steps / e2e_s_max
+    chunks = -(-count // 8192)
+
+    # quick self-check of the timed output against nothing but its own shape
+    if not np.isfinite(out_host).all():
+        raise RuntimeError("non-finite features in the host-ABI output")
+
+    clk = clocks.summary()
+    clocks.close()
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, clk)
+        if clk is not None:
+            mhz = [g["sm_mhz"] for g in gathered if g and g["sm_mhz"] is not None]
+            clk = dict(clk)
+            clk["sm_mhz"] = statistics.median(mhz) if mhz else None
+            clk["reasons"] = sorted({r for g in gathered if g for r in g["reasons"]})
+            clk["per_rank_sm_mhz"] = [g["sm_mhz"] if g else None for g in gathered]
+
+    if rank != 0:
+        return
+    avg_launch_s = kernel_s / args.steps
+    peak, peak_kind = measured_hbm_peak()
+    achieved = count * tb.BYTES_PER_SAMPLE / avg_launch_s / 1e9
+    tps = profiled_traffic_per_sample()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": 1e3 * kernel_s_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded SplitMix64 generator, BASELINE value model)",
+        "config": workload_config(args, world),
+        "e2e": {"value": e2e_value, "unit": UNIT,
+                "h2d_bytes_per_step": count * (tb.OBS_DIM * 4 + tb.MISSION_DIM * 4 + tb.CAMERA_BYTES),
+                "d2h_bytes_per_step": count * tb.FEATURE_DIM * 4,
+                "ms_per_step": 1e3 * e2e_s_max / e2e_steps, "steps": e2e_steps,
+                "api": "tb_cuda_extract_features_host, page-locked host buffers, host wall clock "
+                       "(the call returns after its stream sync), max over ranks"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                     "traffic": (tps * count) if tps else None,
+                     "algorithmic_bytes_per_launch": count * tb.BYTES_PER_SAMPLE,
+                     "kernel": "features_staged_kernel", "avg_launch_ms": avg_launch_s * 1e3},
+        "gpu_launches": args.steps + e2e_steps * chunks,
+        "gpu_launches_detail": {"value_region": args.steps, "e2e_region": e2e_steps * chunks},
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = time_reference_cpu(obs, mission, cams, args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world != 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

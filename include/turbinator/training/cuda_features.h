@@ -1,0 +1,83 @@
+/*
+ * Batched 142-value sensor features on NVIDIA B200 (sm_100a).
+ *
+ * Drop-in replacement for the reference's C ABI
+ * include/turbinator/training/cuda_features.h:1-40 (Viatreen/Turbinator_C).
+ * The six reference entry points keep their names, argument meaning, return
+ * values and error strings.  Entries below "Additive entry points" do not
+ * exist in the reference and change nothing about the six.
+ *
+ * Layouts (row-major, one row per aircraft):
+ *   obs       [batch, 4148] float   48 proprioception, 4096 LiDAR bins, 4 scan-status
+ *   mission   [batch, 10]   float
+ *   cameras   [batch, 16384] uint8  4 cameras x 64 x 64 luma
+ *   features  [batch, 142]  float
+ * Float pointers must be 4-byte aligned.  obs and cameras rows that start on
+ * 16-byte boundaries (any cudaMalloc'd base) take the staged bulk-copy
+ * kernel; other alignments take a slower kernel with the same results.
+ */
+#ifndef TURBINATOR_CUDA_FEATURES_H
+#define TURBINATOR_CUDA_FEATURES_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Replaces cuda_features.h:14-19 (reference src/cuda/features.cu:158-169).
+ * Device pointers; cameras may be NULL (camera features are then 0).
+ * stream is a cudaStream_t or NULL for the legacy default stream.
+ * Returns 1 if the kernel launch succeeded, 0 on NULL obs/mission/features,
+ * batch 0, batch > 0x7fffffff, a float pointer that is not 4-byte aligned,
+ * or a launch error.  Asynchronous: synchronize before reading features. */
+int tb_cuda_extract_features_device(const float *device_obs,
+                                    const float *device_mission,
+                                    const unsigned char *device_cameras,
+                                    float *device_features,
+                                    size_t batch_size,
+                                    void *stream);
+
+/* Replaces cuda_features.h:20 (features.cu:171-173).  Returns 1 when the
+ * stream drained without error.  It also returns 0 (once) when a feature
+ * kernel on the current device gave up waiting on its staging pipeline;
+ * such a launch leaves its features incomplete. */
+int tb_cuda_synchronize(void *stream);
+
+typedef struct tb_cuda_feature_batch tb_cuda_feature_batch;
+
+/* Replaces cuda_features.h:26 (features.cu:27-44).  Makes device_id current
+ * on the calling thread and allocates device staging for max_batch samples.
+ * The reference capped max_batch at 1024; here any max_batch whose staging
+ * fits in device memory is accepted (0 is still rejected).  NULL on
+ * failure. */
+tb_cuda_feature_batch *tb_cuda_feature_batch_create(int device_id, size_t max_batch);
+
+/* Replaces cuda_features.h:27 (features.cu:46-56).  NULL-safe; drains the
+ * handle's streams before freeing. */
+void tb_cuda_feature_batch_destroy(tb_cuda_feature_batch *batch);
+
+/* Replaces cuda_features.h:28 (features.cu:58-60).  "stage: cuda error" of
+ * the last failed host call, "" after a successful one, and
+ * "CUDA feature batch unavailable" for a NULL handle. */
+const char *tb_cuda_feature_batch_error(const tb_cuda_feature_batch *batch);
+
+/* Replaces cuda_features.h:29-34 (features.cu:62-88).  Host pointers;
+ * cameras are required.  0 < count <= max_batch.  Copies in, extracts and
+ * copies out, returning after the features are in out_features_142.
+ * Page-locked host buffers are streamed in chunks so that copies and
+ * kernels overlap; pageable buffers work too, at pageable copy speed.
+ * Returns 1, or 0 with a stage-named message in
+ * tb_cuda_feature_batch_error().  A handle is not thread-safe. */
+int tb_cuda_extract_features_host(tb_cuda_feature_batch *batch,
+                                  const float *obs_4148,
+                                  const float *mission_10,
+                                  const unsigned char *cameras_16384,
+                                  size_t count,
+                                  float *out_features_142);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,48 @@
+/* TEST INFRASTRUCTURE ONLY -- declarations of the CPU oracle and the
+ * multi-threaded CPU baseline runner.  Not part of the shipped library. */
+#ifndef TB_FEATURES_ORACLE_H
+#define TB_FEATURES_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    ORACLE_OBS_DIM = 4148,
+    ORACLE_MISSION_DIM = 10,
+    ORACLE_CAMERA_BYTES = 16384,
+    ORACLE_FEATURE_DIM = 142,
+    ORACLE_SCALARS = 48,
+    ORACLE_LIDAR_OFFSET = 48,
+    ORACLE_TAIL_OFFSET = 4144
+};
+
+/* Same contract as the reference's tb_train_extract_features_cpu
+ * (include/turbinator/training/training.h:55-58). */
+void oracle_extract_features(const float *obs, const float *mission,
+                             const uint8_t *cameras, float *out);
+
+/* Per-sample extractor signature shared by the oracle above and the
+ * reference's own tb_train_extract_features_cpu (loaded from oracle/_ref). */
+typedef void (*oracle_sample_fn)(const float *, const float *, const uint8_t *, float *);
+
+/* Runs `fn` over samples [0, count) of a [count,4148]/[count,10]/[count,16384]
+ * batch with `threads` POSIX threads over contiguous sample ranges, writing
+ * [count,142] features.  cameras may be NULL.  Returns wall seconds, or a
+ * negative value if a thread could not be started. */
+double oracle_extract_batch(oracle_sample_fn fn, const float *obs, const float *mission,
+                            const uint8_t *cameras, size_t count, float *out, int threads);
+
+/* Convenience: oracle_extract_batch with the restated oracle. */
+double oracle_extract_batch_self(const float *obs, const float *mission,
+                                 const uint8_t *cameras, size_t count, float *out,
+                                 int threads);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

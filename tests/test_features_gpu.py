@@ -1,0 +1,181 @@
+"""GPU parity: the sm_100a kernels, called through the C ABI, against the CPU
+oracle (itself pinned to the reference in test_oracle.py).
+
+Exactness classes and tolerances are in tests/parity.py: bit-exact for the
+scalar/mission/camera features, |d| <= 1e-6 + 1e-5*|ref| for LiDAR means.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+import turbinator_c_b200 as tb
+from tests.golden import fixtures
+from tests.parity import check_features
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def run_device(obs, mission, cams, *, stream=None, **opts):
+    """Features via tb_cuda_extract_features_device (or the launch hook with opts)."""
+    n = obs.shape[0]
+    d_obs, d_mis = _dev(obs), _dev(mission)
+    d_cam = _dev(cams) if cams is not None else None
+    d_out = torch.full((n, 142), float("nan"), device="cuda")
+    torch.cuda.synchronize()  # inputs and the NaN fill are complete before any stream reads them
+    if opts:
+        ok = tb.launch(d_obs, d_mis, d_cam, d_out, n, stream, **opts)
+    else:
+        ok = tb.tb_cuda_extract_features_device(d_obs, d_mis, d_cam, d_out, n, stream)
+    assert ok == 1
+    assert tb.tb_cuda_synchronize(stream) == 1
+    return d_out.cpu().numpy()
+
+
+def test_reference_known_answer_via_host_abi():
+    """The reference's own CUDA parity test (tests/test_cuda_features.c:9-56)
+    through the same host entry point, plus the stricter exactness classes."""
+    obs, mission, cams = fixtures.reference_known_answer_inputs()
+    out = np.empty((3, 142), np.float32)
+    with tb.FeatureBatch(int(os.environ.get("TB_CUDA_TEST_DEVICE", "0")), 3) as fb:
+        assert fb.extract(obs, mission, cams, 3, out) == 1, fb.error()
+        assert fb.error() == ""
+    expected = np.load(os.path.join(GOLDEN, "ref_known_answer.npz"))["features"]
+    assert np.all(np.isfinite(out)) and np.max(np.abs(out - expected)) <= 2e-5
+    check_features(out, expected, "known-answer")
+
+
+@pytest.mark.parametrize("name", sorted(fixtures.SEEDED_CASES))
+def test_seeded_goldens(name):
+    seed, total, count, stress = fixtures.SEEDED_CASES[name]
+    obs, mission, cams, _ = tb.generate(seed, 0, count, total=total, stress=stress)
+    expected = np.load(os.path.join(GOLDEN, f"{name}.npz"))["features"]
+    check_features(run_device(obs, mission, cams), expected, name)
+
+
+def test_edge_values_with_and_without_cameras():
+    g = np.load(os.path.join(GOLDEN, "edge_cases.npz"))
+    check_features(run_device(g["obs"], g["mission"], g["cameras"]), g["features"], "edge")
+    check_features(run_device(g["obs"], g["mission"], None), g["features_no_camera"], "edge/no-camera")
+
+
+def test_reference_training_facts_on_gpu():
+    obs = np.zeros((2, 4148), np.float32)
+    mission = np.zeros((2, 10), np.float32)
+    cams = np.full((2, 16384), 128, np.uint8)
+    mission[:, 0] = 1.0
+    obs[:, 2] = 2.0
+    mission[1, 6] = 1.0
+    mission[1, 7] = 0.9
+    f = run_device(obs, mission, cams)
+    assert f[0, 2] > 0 and f[0, 126] > 0 and f[1, 59] == 0.0
+
+
+@pytest.mark.parametrize("config", [1, 2])
+def test_full_config_parity(config):
+    seed, batch, _ = tb.CONFIGS[config]
+    obs, mission, cams, _ = tb.generate(seed, 0, batch)
+    check_features(run_device(obs, mission, cams), oracle.features(obs, mission, cams), f"config{config}")
+
+
+def test_config4_stress_quarters_full_size():
+    seed, batch, _ = tb.CONFIGS[4]
+    obs, mission, cams, _ = tb.generate(seed, 0, batch, stress=True)
+    out = run_device(obs, mission, cams)
+    check_features(out, oracle.features(obs, mission, cams), "config4")
+    q = batch // 4
+    assert np.all(out[0:q:2, 126:] == 0.0) and np.all(out[1:q:2, 126:] == 1.0)  # (a)
+    assert np.all(out[q:2 * q, 62:126] == 1.0)                                   # (b) exactly
+    d = out[3 * q:, 62:126]
+    assert np.all(d == d[0, 0])                                                   # (d) identical
+
+
+@pytest.mark.parametrize("batch", [1, 2, 3, 7, 147, 148, 149, 295, 296, 297, 1023, 1025])
+def test_ragged_batch_sizes(batch):
+    obs, mission, cams, _ = tb.generate(21, 0, batch)
+    check_features(run_device(obs, mission, cams), oracle.features(obs, mission, cams), f"B={batch}")
+
+
+@pytest.mark.parametrize("grid_limit", [1, 2, 5])
+def test_many_samples_per_cta_ring_wraparound(grid_limit):
+    """Few CTAs -> each walks the shared-memory ring many times (phase flips)."""
+    obs, mission, cams, _ = tb.generate(22, 0, 301)
+    out = run_device(obs, mission, cams, grid_limit=grid_limit)
+    check_features(out, oracle.features(obs, mission, cams), f"grid={grid_limit}")
+
+
+def test_direct_kernel_and_unaligned_rows():
+    obs, mission, cams, _ = tb.generate(23, 0, 200)
+    expected = oracle.features(obs, mission, cams)
+    check_features(run_device(obs, mission, cams, force_direct=True), expected, "direct")
+    # rows that start 4 bytes past a 16-byte boundary take the direct kernel
+    n = obs.shape[0]
+    flat = torch.zeros(n * 4148 + 1, device="cuda")
+    flat[1:] = _dev(obs).reshape(-1)
+    camflat = torch.zeros(n * 16384 + 3, dtype=torch.uint8, device="cuda")
+    camflat[3:] = _dev(cams).reshape(-1)
+    d_out = torch.zeros((n, 142), device="cuda")
+    assert tb.tb_cuda_extract_features_device(flat.data_ptr() + 4, _dev(mission), camflat.data_ptr() + 3,
+                                              d_out, n) == 1
+    assert tb.tb_cuda_synchronize() == 1
+    check_features(d_out.cpu().numpy(), expected, "unaligned")
+
+
+def test_non_default_stream_and_null_stream():
+    obs, mission, cams, _ = tb.generate(24, 0, 513)
+    expected = oracle.features(obs, mission, cams)
+    s = torch.cuda.Stream()
+    check_features(run_device(obs, mission, cams, stream=s), expected, "stream")
+    check_features(run_device(obs, mission, cams, stream=None), expected, "legacy stream")
+
+
+def test_host_abi_contract():
+    obs, mission, cams, _ = tb.generate(25, 0, 2500)
+    expected = oracle.features(obs, mission, cams)
+    with tb.FeatureBatch(0, 2500) as fb:  # above the reference's old 1024 cap
+        out = np.zeros((2500, 142), np.float32)
+        assert fb.extract(obs, mission, cams, 2500, out) == 1, fb.error()
+        check_features(out, expected, "host")
+        part = np.zeros((17, 142), np.float32)
+        assert fb.extract(obs[100:117], mission[100:117], cams[100:117], 17, part) == 1
+        check_features(part, expected[100:117], "host/part")
+        assert fb.extract(obs, mission, cams, 2501, out) == 0          # count > max_batch
+        assert fb.extract(obs, mission, None, 10, out) == 0           # cameras required
+        assert fb.extract(obs, mission, cams, 0, out) == 0
+    assert tb.tb_cuda_feature_batch_create(0, 0) is None
+    assert tb.tb_cuda_feature_batch_create(10_000, 4) is None           # invalid device
+
+
+def test_host_abi_pinned_and_chunked():
+    """Page-locked buffers take the streamed, chunked path (> 1 chunk here)."""
+    n = 20000
+    obs, mission, cams, _ = tb.generate(26, 0, n, pinned=True)
+    out = torch.zeros((n, 142), dtype=torch.float32, pin_memory=True).numpy()
+    with tb.FeatureBatch(0, n) as fb:
+        assert fb.extract(obs, mission, cams, n, out) == 1, fb.error()
+    check_features(out, oracle.features(np.asarray(obs), np.asarray(mission), np.asarray(cams)), "pinned")
+
+
+def test_bounded_pipeline_wait_reports_and_recovers():
+    """A sample whose copies are withheld makes the consumers' bounded waits
+    expire: the launch ends, tb_cuda_synchronize reports it once, and the
+    device keeps working."""
+    obs, mission, cams, _ = tb.generate(27, 0, 64)
+    d_obs, d_mis, d_cam = _dev(obs), _dev(mission), _dev(cams)
+    d_out = torch.zeros((64, 142), device="cuda")
+    assert tb.take_status() == 0
+    assert tb.launch(d_obs, d_mis, d_cam, d_out, 64, None, wait_ns=20_000_000, stall_sample=5) == 1
+    assert tb.tb_cuda_synchronize() == 0
+    assert tb.tb_cuda_synchronize() == 1          # reported once, then cleared
+    check_features(run_device(obs, mission, cams), oracle.features(obs, mission, cams), "after-timeout")

@@ -1,0 +1,47 @@
+"""Seeded synthetic batches: determinism, shard independence, value model."""
+from __future__ import annotations
+
+import numpy as np
+
+import turbinator_c_b200 as tb
+
+
+def test_shards_regenerate_identically():
+    full = tb.generate(7, 0, 96, f32_cameras=True)
+    part = tb.generate(7, 40, 30, total=96, f32_cameras=True)
+    for a, b in zip(full, part):
+        assert np.array_equal(a[40:70], b)
+    again = tb.generate(7, 0, 96, threads=3, f32_cameras=True)
+    for a, b in zip(full, again):
+        assert np.array_equal(a, b)
+
+
+def test_value_model():
+    obs, mission, cams, camf = tb.generate(2, 0, 256, f32_cameras=True)
+    lidar = obs[:, 48:4144]
+    assert np.all((lidar >= 0.5) & (lidar <= 300.0))
+    frac_noreturn = np.mean(lidar == 300.0)
+    assert 0.04 < frac_noreturn < 0.06
+    for block in (obs[:, :48], obs[:, 4144:], mission):
+        assert np.all(np.abs(block) <= 1.0)
+    assert np.all((camf >= 0) & (camf <= 1))
+    q = np.floor(np.clip(camf, 0, 1) * np.float32(255) + np.float32(0.5)).astype(np.uint8)
+    assert np.array_equal(q, cams)
+    rows = camf.reshape(-1, 4, 64, 64).mean(axis=(0, 1, 3))
+    assert abs(rows[0] - 0.8) < 0.01 and abs(rows[63] - 0.2) < 0.01
+    assert 0.2 < np.mean(mission[:, 6] > 0.5) < 0.3
+
+
+def test_stress_quarters():
+    obs, mission, cams, _ = tb.generate(4, 0, 128, total=128, stress=True)
+    a, b, c, d = (slice(0, 32), slice(32, 64), slice(64, 96), slice(96, 128))
+    assert np.all(cams[a][0::2] == 0) and np.all(cams[a][1::2] == 255)
+    assert np.all(obs[b, 48:4144] == 300.0)
+    assert np.all(obs[d, 48:4144] == 0.5)
+    lid = obs[c, 48:4144].reshape(32, 2, 4, 4, 8, 16)  # head, el_sector, row, az_sector, bin
+    sectors = lid.transpose(0, 1, 2, 4, 3, 5).reshape(32, 64, 64)
+    mins = sectors.min(axis=2, keepdims=True)
+    assert np.all((sectors == mins).sum(axis=2) >= 3)
+    # a shard of the stress batch reproduces the same quarters
+    part = tb.generate(4, 60, 40, total=128, stress=True)
+    assert np.array_equal(part[0], obs[60:100]) and np.array_equal(part[2], cams[60:100])

@@ -1,0 +1,571 @@
+/*
+ * sm_100a kernels for the 142 sensor features, plus the thin extern "C"
+ * launch shim that replaces the reference's device entry points
+ * (Viatreen/Turbinator_C src/cuda/features.cu:90-173).
+ *
+ * What is computed per aircraft (reference CPU path training.c:102-142):
+ *   f[0..47]    clamp(finite(obs[i]) / divisor_i, -1, 1)
+ *   f[48..51]   clamp(finite(obs[4144+i]), 0, 1)
+ *   f[52..61]   clamp(finite(mission[i]), -1, 1); 59..61 are 0 when
+ *               finite(mission[6]) > 0.5 (arena: opponent truth hidden)
+ *   f[62..125]  mean over a 4x16 LiDAR sector of
+ *               (-1 if !finite(r) or r < 0, else log1p(min(r,120))/log1p(120))
+ *   f[126..141] camera quadrant byte sum / (1024 * 255)
+ *
+ * Design (B200):
+ *  - The path is a streaming reduction: 33,016 bytes in and 568 bytes out
+ *    per aircraft, ~1 flop per byte.  It is bound by HBM bandwidth, so the
+ *    kernel is built to keep enough bytes in flight and to touch every byte
+ *    exactly once.
+ *  - Persistent CTAs (grid = SMs x resident CTAs) with one producer warp and
+ *    eight consumer warps.  The producer streams each aircraft's
+ *    observation row (16,592 B) and camera block (16,384 B) into a
+ *    shared-memory ring with 1-D bulk copies (cp.async.bulk, completion
+ *    counted in bytes on an mbarrier) and its 40-byte mission row with
+ *    4-byte cp.async tracked on the same mbarrier.  No multicast anywhere.
+ *  - The eight consumer warps reduce one staged aircraft together.  Warp w
+ *    owns LiDAR rows 4w..4w+3 (one head x elevation-sector band, i.e. eight
+ *    sectors) and half-camera w (camera w/2, rows 32*(w&1)..+31); all
+ *    shared-memory reads are 128-bit and conflict-free.  Per-sector and
+ *    per-quadrant partials are combined with warp shuffles.
+ *  - Exactness: the scalar, mission and camera features are bit-identical
+ *    to the reference (IEEE division, integer byte sums, the reference's
+ *    compare-based clamp).  A LiDAR sector mean is computed as
+ *    (n_saturated - n_invalid + K * sum log2(1 + r)) / 64 over the
+ *    in-range bins, with K = 1/log2(121).  Saturated (>= 120 m) and invalid
+ *    bins therefore contribute exact integers -- an all-no-return sector is
+ *    exactly 1.0 and an all-invalid one exactly -1.0, as in the reference --
+ *    and only in-range bins carry the lg2 approximation error (well inside
+ *    the 1e-6 absolute / 1e-5 relative tolerance of the parity tests).
+ *  - Every mbarrier wait is bounded (about one second of %globaltimer);
+ *    on expiry the kernel records a status bit that tb_cuda_synchronize()
+ *    reports, drains its own outstanding copies (bounded again) and exits.
+ */
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <stdint.h>
+
+#include "turbinator/training/cuda_features.h"
+#include "tb_features_internal.h"
+
+namespace {
+
+constexpr int kObsDim = 4148;
+constexpr int kMissionDim = 10;
+constexpr int kCameraBytes = 16384;
+constexpr int kFeatureDim = 142;
+constexpr int kLidarOffset = 48;
+constexpr int kTailOffset = 4144;
+
+constexpr uint32_t kObsBytes = kObsDim * 4u;                  /* 16,592 = 16 * 1,037 */
+constexpr uint32_t kStageCamOff = kObsBytes;                  /* 16-byte aligned */
+constexpr uint32_t kStageMissionOff = kStageCamOff + kCameraBytes; /* 32,976 */
+constexpr uint32_t kStageBytes = 33024;                       /* 258 * 128 */
+static_assert(kStageMissionOff + kMissionDim * 4 <= kStageBytes, "stage layout");
+static_assert(kObsBytes % 16 == 0 && kCameraBytes % 16 == 0, "bulk copy sizes");
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = 32 * (kConsumerWarps + 1);
+constexpr int kStages = 3;
+constexpr uint32_t kBarrierRegion = 128;
+constexpr uint32_t kSmemBytes = kBarrierRegion + kStages * kStageBytes;
+
+/* 1 / log2(121): a LiDAR term log1p(x)/log1p(120) equals log2(1+x) times this. */
+constexpr float kInvLog2_121 = 0.14453241315894394f;
+
+constexpr unsigned long long kDefaultWaitNs = 1000000000ull; /* ~1 s per wait */
+
+/* ------------------------------------------------------------------ */
+/* Sticky per-device status word, read and cleared by tb_cuda_synchronize. */
+__device__ unsigned int g_feature_status;
+
+/* ------------------------------------------------------------------ */
+/* PTX wrappers (sm_90+ forms, valid on sm_100a). */
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+/* Bounded wait for the phase with the given parity; false on timeout. */
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          unsigned long long limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > limit_ns) return false;
+    }
+}
+
+/* 1-D bulk copy global -> this CTA's shared memory, completion counted on
+ * `bar` in bytes.  src, dst and bytes are multiples of 16. */
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
+                                          uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+
+/* 4-byte asynchronous copy (mission entries: rows are only 8-byte aligned). */
+__device__ __forceinline__ void async_load4(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+
+/* Make `bar` track completion of this thread's prior cp.async copies. */
+__device__ __forceinline__ void async_track(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+/* ------------------------------------------------------------------ */
+/* Per-feature arithmetic shared by both kernels. */
+
+/* Reference training.c:57-59 clamp; the compare form fixes zero signs. */
+__device__ __forceinline__ float clamp_ref(float x, float lo, float hi) {
+    return x < lo ? lo : (x > hi ? hi : x);
+}
+
+__device__ __forceinline__ float finite_or_zero(float x) {
+    return isfinite(x) ? x : 0.0f;
+}
+
+/* Divisors of the 48 proprioceptive values (training.c:70-81). */
+__device__ __forceinline__ float scalar_divisor(int i) {
+    const float pi = 3.14159265358979323846f;
+    float d = 1.0f;
+    d = (i <= 1) ? 300.0f : d;
+    d = (i == 2) ? 100.0f : d;
+    d = (i >= 3 && i <= 5) ? 50.0f : d;
+    d = (i >= 10 && i <= 12) ? 5.0f : d;
+    d = (i >= 13 && i <= 15) ? 30.0f : d;
+    d = (i >= 28 && i <= 31) ? pi / 4.0f : d;
+    d = (i >= 32 && i <= 39) ? 5.0f : d;
+    d = (i == 44 || i == 45) ? pi / 2.0f : d;
+    return d;
+}
+
+/* Feature t in [0, 62) from the observation row `o` and mission row `m`. */
+__device__ __forceinline__ float scalar_feature(int t, const float *o, const float *m) {
+    if (t < 48) return clamp_ref(__fdiv_rn(finite_or_zero(o[t]), scalar_divisor(t)), -1.0f, 1.0f);
+    if (t < 52) return clamp_ref(finite_or_zero(o[kTailOffset + t - 48]), 0.0f, 1.0f);
+    const int i = t - 52;
+    const bool arena = finite_or_zero(m[6]) > 0.5f;
+    const float v = (i >= 7 && arena) ? 0.0f : m[i];
+    return clamp_ref(finite_or_zero(v), -1.0f, 1.0f);
+}
+
+/* LiDAR sector accumulator: `sum` adds log2(1+r) over bins with
+ * 0 <= r < 120; `counts` packs n_in_range (low byte) and n_saturated
+ * (120 <= r < inf, second byte).  Invalid bins (NaN, +-inf, r < 0) are
+ * 64 - n_in_range - n_saturated. */
+__device__ __forceinline__ void lidar_bin(float r, float &sum, int &counts) {
+    const bool in_range = (r >= 0.0f) && (r < 120.0f);
+    const bool saturated = (r >= 120.0f) && (r < __int_as_float(0x7f800000));
+    const float lg = __log2f(1.0f + r);
+    sum += in_range ? lg : 0.0f;
+    counts += (in_range ? 1 : 0) + (saturated ? 256 : 0);
+}
+
+__device__ __forceinline__ void lidar_bins4(const float4 v, float &sum, int &counts) {
+    lidar_bin(v.x, sum, counts);
+    lidar_bin(v.y, sum, counts);
+    lidar_bin(v.z, sum, counts);
+    lidar_bin(v.w, sum, counts);
+}
+
+/* Mean of a 64-bin sector from its reduced accumulator. */
+__device__ __forceinline__ float lidar_sector_mean(float sum, int counts) {
+    const int n_in = counts & 255;
+    const int n_sat = counts >> 8;
+    const float integral = static_cast<float>(2 * n_sat + n_in - 64); /* n_sat - n_invalid */
+    return __fmaf_rn(sum, kInvLog2_121, integral) * (1.0f / 64.0f);
+}
+
+__device__ __forceinline__ float camera_feature(unsigned int sum) {
+    return __fdiv_rn(static_cast<float>(sum), 1024.0f * 255.0f);
+}
+
+__device__ __forceinline__ uint32_t byte_sum4(uint32_t w, uint32_t acc) {
+    return __dp4a(w, 0x01010101u, acc);
+}
+
+/* ------------------------------------------------------------------ */
+/* Staged kernel: persistent, warp-specialised, bulk-copy pipeline. */
+
+struct StagedArgs {
+    const float *obs;
+    const float *mission;
+    const unsigned char *cameras; /* may be NULL */
+    float *features;
+    unsigned long long batch;
+    unsigned long long wait_ns;
+    long long stall_sample; /* test hook: >= 0 withholds that sample's copies */
+};
+
+__global__ void __launch_bounds__(kThreads, 2) features_staged_kernel(const StagedArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const uint32_t full_bar = smem_addr(smem);            /* kStages x 8 B */
+    const uint32_t empty_bar = full_bar + 8 * kStages;     /* kStages x 8 B */
+    unsigned char *stages = smem + kBarrierRegion;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full_bar + 8 * s, 1);
+            mbar_init(empty_bar + 8 * s, kConsumerWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    const unsigned long long first = blockIdx.x;
+    const unsigned long long step = gridDim.x;
+
+    if (warp == kConsumerWarps) {
+        /* ---------------- producer warp ---------------- */
+        const uint64_t policy = evict_first_policy();
+        const uint32_t tx_bytes = kObsBytes + (a.cameras ? kCameraBytes : 0u);
+        unsigned long long k = 0;
+        bool ok = true;
+        for (unsigned long long sample = first; sample < a.batch; sample += step, ++k) {
+            const int s = static_cast<int>(k % kStages);
+            const uint32_t phase = static_cast<uint32_t>((k / kStages) & 1);
+            if (!mbar_wait(empty_bar + 8 * s, phase ^ 1u, a.wait_ns)) { ok = false; break; }
+            if (static_cast<long long>(sample) == a.stall_sample) continue; /* test hook */
+            const uint32_t stage = smem_addr(stages + static_cast<size_t>(s) * kStageBytes);
+            if (lane < kMissionDim) {
+                async_load4(stage + kStageMissionOff + 4 * lane,
+                            a.mission + sample * kMissionDim + lane);
+                async_track(full_bar + 8 * s);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive_expect_tx(full_bar + 8 * s, tx_bytes);
+                bulk_load(stage, a.obs + sample * kObsDim, kObsBytes, full_bar + 8 * s, policy);
+                if (a.cameras)
+                    bulk_load(stage + kStageCamOff, a.cameras + sample * kCameraBytes, kCameraBytes,
+                              full_bar + 8 * s, policy);
+            }
+            __syncwarp();
+        }
+        if (!ok) {
+            if (lane == 0) atomicOr(&g_feature_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
+            /* Drain this CTA's outstanding copies before exiting (bounded). */
+            const unsigned long long issued = k;
+            const unsigned long long lo = issued > kStages ? issued - kStages : 0;
+            for (unsigned long long j = lo; j < issued; ++j)
+                mbar_wait(full_bar + 8 * (j % kStages), static_cast<uint32_t>((j / kStages) & 1),
+                          a.wait_ns);
+        }
+        return;
+    }
+
+    /* ---------------- consumer warps ---------------- */
+    const int head = warp >> 2;          /* LiDAR rows 4w..4w+3 = head, elevation sector */
+    const int el_sector = warp & 3;
+    const int cam = warp >> 1;           /* camera half-image w */
+    const int qy = warp & 1;
+    unsigned long long k = 0;
+    for (unsigned long long sample = first; sample < a.batch; sample += step, ++k) {
+        const int s = static_cast<int>(k % kStages);
+        const uint32_t phase = static_cast<uint32_t>((k / kStages) & 1);
+        if (!mbar_wait(full_bar + 8 * s, phase, a.wait_ns)) {
+            if (lane == 0) atomicOr(&g_feature_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
+            return;
+        }
+        const unsigned char *stage = stages + static_cast<size_t>(s) * kStageBytes;
+        const float *o = reinterpret_cast<const float *>(stage);
+        const float *m = reinterpret_cast<const float *>(stage + kStageMissionOff);
+
+        /* LiDAR: lane covers bins 4*lane..4*lane+3 of the warp's four rows;
+         * all 16 values belong to sector (head, el_sector, lane/4). */
+        const float4 *rows = reinterpret_cast<const float4 *>(o + kLidarOffset) +
+                             (head * 16 + el_sector * 4) * 32 + lane;
+        const float4 r0 = rows[0], r1 = rows[32], r2 = rows[64], r3 = rows[96];
+
+        /* Camera half-image: lane reads 16-byte chunks lane, lane+32, ...;
+         * chunk c sits in row c/4, columns 16*(c%4).., so quadrant x = bit 1. */
+        uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0, c2 = c0, c3 = c0;
+        if (a.cameras) {
+            const uint4 *half = reinterpret_cast<const uint4 *>(stage + kStageCamOff) +
+                                cam * 256 + qy * 128 + lane;
+            c0 = half[0]; c1 = half[32]; c2 = half[64]; c3 = half[96];
+        }
+        float scalar = 0.0f;
+        const int t = warp * 32 + lane;
+        if (t < 62) scalar = scalar_feature(t, o, m);
+
+        /* All shared-memory reads of this stage are done: release it. */
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar + 8 * s);
+
+        float sum = 0.0f;
+        int counts = 0;
+        lidar_bins4(r0, sum, counts);
+        lidar_bins4(r1, sum, counts);
+        lidar_bins4(r2, sum, counts);
+        lidar_bins4(r3, sum, counts);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        counts += __shfl_xor_sync(0xffffffffu, counts, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        counts += __shfl_xor_sync(0xffffffffu, counts, 2);
+
+        uint32_t bytes = 0;
+        bytes = byte_sum4(c0.x, bytes); bytes = byte_sum4(c0.y, bytes);
+        bytes = byte_sum4(c0.z, bytes); bytes = byte_sum4(c0.w, bytes);
+        bytes = byte_sum4(c1.x, bytes); bytes = byte_sum4(c1.y, bytes);
+        bytes = byte_sum4(c1.z, bytes); bytes = byte_sum4(c1.w, bytes);
+        bytes = byte_sum4(c2.x, bytes); bytes = byte_sum4(c2.y, bytes);
+        bytes = byte_sum4(c2.z, bytes); bytes = byte_sum4(c2.w, bytes);
+        bytes = byte_sum4(c3.x, bytes); bytes = byte_sum4(c3.y, bytes);
+        bytes = byte_sum4(c3.z, bytes); bytes = byte_sum4(c3.w, bytes);
+        bytes += __shfl_xor_sync(0xffffffffu, bytes, 1);
+        bytes += __shfl_xor_sync(0xffffffffu, bytes, 4);
+        bytes += __shfl_xor_sync(0xffffffffu, bytes, 8);
+        bytes += __shfl_xor_sync(0xffffffffu, bytes, 16);
+
+        float *f = a.features + sample * kFeatureDim;
+        if ((lane & 3) == 0)
+            f[62 + head * 32 + el_sector * 8 + (lane >> 2)] = lidar_sector_mean(sum, counts);
+        if (lane == 0 || lane == 2)
+            f[126 + cam * 4 + qy * 2 + (lane >> 1)] = camera_feature(bytes);
+        if (t < 62) f[t] = scalar;
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* Direct kernel for rows that are not 16-byte aligned: one warp per
+ * aircraft, plain loads, same arithmetic. */
+
+__global__ void __launch_bounds__(256) features_direct_kernel(const float *obs, const float *mission,
+                                                              const unsigned char *cameras,
+                                                              float *features,
+                                                              unsigned long long batch) {
+    const int lane = threadIdx.x & 31;
+    const unsigned long long warps = (static_cast<unsigned long long>(gridDim.x) * blockDim.x) >> 5;
+    for (unsigned long long sample = (static_cast<unsigned long long>(blockIdx.x) * blockDim.x +
+                                      threadIdx.x) >> 5;
+         sample < batch; sample += warps) {
+        const float *o = obs + sample * kObsDim;
+        const float *m = mission + sample * kMissionDim;
+        float *f = features + sample * kFeatureDim;
+        for (int band = 0; band < 8; ++band) { /* head * 4 + el_sector */
+            float sum = 0.0f;
+            int counts = 0;
+            for (int row = 0; row < 4; ++row) {
+                const float *bins = o + kLidarOffset + (band * 4 + row) * 128 + 4 * lane;
+                lidar_bin(bins[0], sum, counts);
+                lidar_bin(bins[1], sum, counts);
+                lidar_bin(bins[2], sum, counts);
+                lidar_bin(bins[3], sum, counts);
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            counts += __shfl_xor_sync(0xffffffffu, counts, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            counts += __shfl_xor_sync(0xffffffffu, counts, 2);
+            if ((lane & 3) == 0) f[62 + band * 8 + (lane >> 2)] = lidar_sector_mean(sum, counts);
+        }
+        for (int half = 0; half < 8; ++half) { /* camera * 2 + qy */
+            unsigned int bytes = 0;
+            if (cameras) {
+                const unsigned char *px = cameras + sample * kCameraBytes + half * 2048 + 2 * lane;
+                for (int y = 0; y < 32; ++y) bytes += px[y * 64] + px[y * 64 + 1];
+            }
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, 1);
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, 2);
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, 4);
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, 8);
+            if (lane == 0 || lane == 16) f[126 + half * 2 + (lane >> 4)] = camera_feature(bytes);
+        }
+        f[lane] = scalar_feature(lane, o, m);
+        if (lane + 32 < 62) f[lane + 32] = scalar_feature(lane + 32, o, m);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* Per-device launch parameters, filled on first use of each device. */
+
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+    std::atomic<int> ready{0};
+    int sms = 0;
+    int staged_blocks_per_sm = 0;
+};
+DeviceInfo g_devices[kMaxDevices];
+
+cudaError_t device_info(int dev, const DeviceInfo **out) {
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    DeviceInfo &d = g_devices[dev];
+    if (!d.ready.load(std::memory_order_acquire)) {
+        int sms = 0, blocks = 0;
+        cudaError_t st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (st != cudaSuccess) return st;
+        st = cudaFuncSetAttribute(features_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(kSmemBytes));
+        if (st != cudaSuccess) return st;
+        st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, features_staged_kernel, kThreads,
+                                                           kSmemBytes);
+        if (st != cudaSuccess) return st;
+        d.sms = sms;
+        d.staged_blocks_per_sm = blocks > 0 ? blocks : 1;
+        d.ready.store(1, std::memory_order_release);
+    }
+    *out = &d;
+    return cudaSuccess;
+}
+
+bool aligned(const void *p, uintptr_t n) {
+    return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0;
+}
+
+} /* namespace */
+
+/* ------------------------------------------------------------------ */
+/* Internal launch used by the public shim and by the tests' hooks. */
+
+extern "C" int tb_features_launch_checked(const float *obs, const float *mission,
+                                          const unsigned char *cameras, float *features,
+                                          size_t batch, void *stream,
+                                          const tb_features_launch_opts *opts, int *launch_error) {
+    if (launch_error) *launch_error = static_cast<int>(cudaErrorInvalidValue);
+    if (!obs || !mission || !features || batch == 0 || batch > 0x7fffffffu) return 0;
+    if (!aligned(obs, 4) || !aligned(mission, 4) || !aligned(features, 4)) return 0;
+    int dev = 0;
+    cudaError_t st = cudaGetDevice(&dev);
+    const DeviceInfo *info = nullptr;
+    if (st == cudaSuccess) st = device_info(dev, &info);
+    if (st != cudaSuccess) {
+        if (launch_error) *launch_error = static_cast<int>(st);
+        return 0;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    /* Discard an earlier, unrelated error of this thread so that the check
+     * after the launch reports this launch only (a sticky device error
+     * persists and still fails it). */
+    cudaGetLastError();
+    const int force_direct = opts && opts->force_direct;
+    const bool staged = !force_direct && aligned(obs, 16) && (!cameras || aligned(cameras, 16));
+    if (staged) {
+        StagedArgs args;
+        args.obs = obs;
+        args.mission = mission;
+        args.cameras = cameras;
+        args.features = features;
+        args.batch = batch;
+        args.wait_ns = (opts && opts->wait_ns) ? opts->wait_ns : kDefaultWaitNs;
+        args.stall_sample = opts ? opts->stall_sample : -1;
+        unsigned long long grid = static_cast<unsigned long long>(info->sms) *
+                                  static_cast<unsigned long long>(info->staged_blocks_per_sm);
+        if (opts && opts->grid_limit > 0 && grid > static_cast<unsigned long long>(opts->grid_limit))
+            grid = static_cast<unsigned long long>(opts->grid_limit);
+        if (grid > batch) grid = batch;
+        features_staged_kernel<<<static_cast<unsigned int>(grid), kThreads, kSmemBytes, s>>>(args);
+    } else {
+        const unsigned long long warps_needed = batch;
+        unsigned long long grid = (warps_needed + 7) / 8;
+        const unsigned long long cap = static_cast<unsigned long long>(info->sms) * 8;
+        if (grid > cap) grid = cap;
+        features_direct_kernel<<<static_cast<unsigned int>(grid), 256, 0, s>>>(obs, mission, cameras,
+                                                                                features, batch);
+    }
+    st = cudaGetLastError();
+    if (launch_error) *launch_error = static_cast<int>(st);
+    return st == cudaSuccess;
+}
+
+extern "C" int tb_features_launch(const float *obs, const float *mission,
+                                  const unsigned char *cameras, float *features, size_t batch,
+                                  void *stream, const tb_features_launch_opts *opts) {
+    return tb_features_launch_checked(obs, mission, cameras, features, batch, stream, opts, nullptr);
+}
+
+extern "C" int tb_features_status_take(void *stream, unsigned int *status) {
+    unsigned int value = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyFromSymbolAsync(&value, g_feature_status, sizeof(value), 0,
+                                  cudaMemcpyDeviceToHost, s) != cudaSuccess)
+        return 0;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return 0;
+    if (value) {
+        static const unsigned int zero = 0;
+        if (cudaMemcpyToSymbolAsync(g_feature_status, &zero, sizeof(zero), 0,
+                                    cudaMemcpyHostToDevice, s) != cudaSuccess)
+            return 0;
+        if (cudaStreamSynchronize(s) != cudaSuccess) return 0;
+    }
+    if (status) *status = value;
+    return 1;
+}
+
+extern "C" int tb_features_staged_config(int *blocks_per_sm, int *sms, int *smem_bytes,
+                                         int *threads, int *stages) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    const DeviceInfo *info = nullptr;
+    if (device_info(dev, &info) != cudaSuccess) return 0;
+    if (blocks_per_sm) *blocks_per_sm = info->staged_blocks_per_sm;
+    if (sms) *sms = info->sms;
+    if (smem_bytes) *smem_bytes = static_cast<int>(kSmemBytes);
+    if (threads) *threads = kThreads;
+    if (stages) *stages = kStages;
+    return 1;
+}
+
+/* ---- reference entry points (cuda_features.h:14-20) ---- */
+
+extern "C" int tb_cuda_extract_features_device(const float *device_obs, const float *device_mission,
+                                               const unsigned char *device_cameras,
+                                               float *device_features, size_t batch_size,
+                                               void *stream) {
+    return tb_features_launch(device_obs, device_mission, device_cameras, device_features,
+                              batch_size, stream, nullptr);
+}
+
+extern "C" int tb_cuda_synchronize(void *stream) {
+    if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return 0;
+    unsigned int status = 0;
+    if (!tb_features_status_take(stream, &status)) return 0;
+    return status == 0;
+}

@@ -1,0 +1,58 @@
+/*
+ * Internal interface between the C11 host code, the CUDA launch shim and
+ * the tests.  Not part of the public ABI (include/turbinator/...).
+ */
+#ifndef TB_FEATURES_INTERNAL_H
+#define TB_FEATURES_INTERNAL_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    TB_OBS_DIM = 4148,
+    TB_MISSION_DIM = 10,
+    TB_CAMERA_BYTES = 16384,
+    TB_FEATURE_DIM = 142
+};
+
+/* Status bits recorded by the kernels in a per-device word. */
+enum { TB_FEATURE_STATUS_WAIT_TIMEOUT = 1u };
+
+typedef struct tb_features_launch_opts {
+    int force_direct;                 /* 1: use the plain-load kernel even for aligned rows */
+    int grid_limit;                   /* > 0: cap on staged-kernel CTAs */
+    unsigned long long wait_ns;       /* 0: default (~1 s) limit on each pipeline wait */
+    long long stall_sample;           /* test hook: >= 0 withholds that sample's copies so the
+                                         bounded waits expire; -1 in normal use */
+} tb_features_launch_opts;
+
+/* Launch on the current device; same return contract as
+ * tb_cuda_extract_features_device.  opts may be NULL. */
+int tb_features_launch(const float *obs, const float *mission, const unsigned char *cameras,
+                       float *features, size_t batch, void *stream,
+                       const tb_features_launch_opts *opts);
+
+/* As tb_features_launch; on failure *launch_error (if not NULL) receives
+ * the cudaError_t of the failed step (cudaErrorInvalidValue for rejected
+ * arguments). */
+int tb_features_launch_checked(const float *obs, const float *mission,
+                               const unsigned char *cameras, float *features, size_t batch,
+                               void *stream, const tb_features_launch_opts *opts,
+                               int *launch_error);
+
+/* Reads (via `stream`) and clears the current device's kernel status word.
+ * Returns 1 if the read succeeded; *status receives the bits. */
+int tb_features_status_take(void *stream, unsigned int *status);
+
+/* Launch geometry of the staged kernel on the current device. */
+int tb_features_staged_config(int *blocks_per_sm, int *sms, int *smem_bytes, int *threads,
+                              int *stages);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif
