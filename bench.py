@@ -38,7 +38,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 import turbinator_c_b200 as tb  # noqa: E402
-from turbinator_c_b200.shard import shard_range  # noqa: E402
+from turbinator_c_b200.shard import max_over_ranks, shard_range  # noqa: E402
 
 METRIC = "sensor-feature samples/sec"
 UNIT = "samples/s"
@@ -266,13 +266,6 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     clocks = ClockSampler(local_rank)
 

@@ -45,3 +45,18 @@ def gather_features(local: np.ndarray, total: int, group=None, dst: int = 0):
     if rank != dst:
         return None
     return np.concatenate([p[:c].cpu().numpy() for p, c in zip(parts, counts)], axis=0)
+
+
+def max_over_ranks(value: float, group=None) -> float:
+    """The largest of every rank's `value` (used for timed regions: a job is as
+    slow as its slowest GPU).  Single-process runs return `value`."""
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return value
+    device = (torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl"
+              else torch.device("cpu"))
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return float(t.item())
