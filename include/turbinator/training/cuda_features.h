@@ -76,6 +76,37 @@ int tb_cuda_extract_features_host(tb_cuda_feature_batch *batch,
                                   size_t count,
                                   float *out_features_142);
 
+/* ---- Additive entry points ---- */
+
+/* Largest count accepted by tb_cuda_extract_features_host_noalloc. */
+#define TB_CUDA_NOALLOC_MAX_BATCH 64
+
+/* No counterpart in the reference.  For callers that cannot allocate device
+ * memory: an onboard control loop that forbids allocation once it is running
+ * (cudaMalloc can block and synchronise the device in the middle of a tick),
+ * or a process whose GPU memory is already reserved in full by a learner's
+ * memory pool.  Does the work of tb_cuda_extract_features_host without a
+ * handle: the rows are staged through one fixed 2,149,376-byte array that the
+ * library reserves statically on every GPU that loads it (held until the
+ * process exits); nothing here calls cudaMalloc or cudaFree.
+ * Host pointers; cameras required; stream is a cudaStream_t or NULL; uses the
+ * calling thread's current device.  Blocks until the features are in
+ * out_features_142.  Returns 1 on success; -1, doing nothing, when count is 0
+ * or greater than TB_CUDA_NOALLOC_MAX_BATCH; 0 on a NULL pointer or a CUDA
+ * error.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls on a device share the one array, which keeps the last call's rows:
+ * calls that overlap on the GPU (several host threads at once) race.  Each
+ * call overwrites every row it reads, so nothing needs clearing between
+ * calls. */
+int tb_cuda_extract_features_host_noalloc(const float *obs_4148,
+                                          const float *mission_10,
+                                          const unsigned char *cameras_16384,
+                                          size_t count,
+                                          float *out_features_142,
+                                          void *stream);
+
 #ifdef __cplusplus
 }
 #endif

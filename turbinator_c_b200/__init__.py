@@ -75,6 +75,7 @@ def load_library() -> ctypes.CDLL:
     _bind(lib, "tb_cuda_feature_batch_destroy", None, [_vp])
     _bind(lib, "tb_cuda_feature_batch_error", _c.c_char_p, [_vp])
     _bind(lib, "tb_cuda_extract_features_host", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
+    _bind(lib, "tb_cuda_extract_features_host_noalloc", _c.c_int, [_vp, _vp, _vp, _sz, _vp, _vp])
     _bind(lib, "tb_features_launch", _c.c_int,
           [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_status_take", _c.c_int, [_vp, _c.POINTER(_c.c_uint)])
@@ -133,6 +134,21 @@ def tb_cuda_extract_features_host(handle: Optional[int], obs, mission, cameras, 
                                   out_features) -> int:
     return load_library().tb_cuda_extract_features_host(
         handle, _ptr(obs), _ptr(mission), _ptr(cameras), count, _ptr(out_features))
+
+
+# ---- additive entry points ----
+
+#: Largest count accepted by tb_cuda_extract_features_host_noalloc (cuda_features.h).
+NOALLOC_MAX_BATCH = 64
+
+
+def tb_cuda_extract_features_host_noalloc(obs, mission, cameras, count: int, out_features,
+                                          stream=None) -> int:
+    """Handle-free host extraction staged through the library's fixed device
+    array (for callers that cannot allocate device memory).  1 = success,
+    -1 = count is 0 or above NOALLOC_MAX_BATCH, 0 = NULL pointer or CUDA error."""
+    return load_library().tb_cuda_extract_features_host_noalloc(
+        _ptr(obs), _ptr(mission), _ptr(cameras), count, _ptr(out_features), _stream_handle(stream))
 
 
 # ---- internal hooks used by tests and the benchmark ----
