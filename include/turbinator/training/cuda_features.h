@@ -78,6 +78,24 @@ int tb_cuda_extract_features_host(tb_cuda_feature_batch *batch,
 
 /* ---- Additive entry points ---- */
 
+/* Onboard tactical (24) and physics-prior (15) values per aircraft: the
+ * reference's device-only src/network/onboard_features.cuh:515-519
+ * (tb_onboard_tactical_prior), which its 618M learner evaluates one thread
+ * per aircraft (src/network/network_gpu.cu:274-303) and which
+ * tests/test_onboard_features.cu checks.  No C entry point exists for it in
+ * the reference; this one follows the conventions of
+ * tb_cuda_extract_features_device.  Device pointers: obs [batch,4148],
+ * mission [batch,10], tactical [batch,24], prior [batch,15] (rows of 24 and
+ * 15 floats).  Returns 1 if the launch succeeded, 0 on NULL pointers, batch
+ * 0 or > 0x7fffffff, a pointer that is not 4-byte aligned, or a launch
+ * error.  Asynchronous on `stream` (NULL = legacy default stream). */
+int tb_cuda_extract_onboard_device(const float *device_obs,
+                                   const float *device_mission,
+                                   float *device_tactical_24,
+                                   float *device_prior_15,
+                                   size_t batch_size,
+                                   void *stream);
+
 /* Largest count accepted by tb_cuda_extract_features_host_noalloc. */
 #define TB_CUDA_NOALLOC_MAX_BATCH 64
 

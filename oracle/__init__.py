@@ -19,12 +19,14 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_PATH = os.path.join(HERE, "liboracle.so")
 REF_TRAINING_PATH = os.path.join(HERE, "_ref", "libtb_ref_training.so")
 REF_ONBOARD_PATH = os.path.join(HERE, "_ref", "libtb_ref_onboard.so")
+REF_ONBOARD_CR_PATH = os.path.join(HERE, "_ref", "libtb_ref_onboard_cr.so")
 
 _vp = ctypes.c_void_p
 _sz = ctypes.c_size_t
 _oracle = None
 _ref_training = None
 _ref_onboard = None
+_ref_onboard_cr = None
 
 
 def _addr(a) -> Optional[int]:
@@ -129,4 +131,26 @@ def onboard_reference(obs, mission):
     assert mission.dtype == np.float32 and mission.shape == (n, 10) and mission.flags.c_contiguous
     out = np.empty((n, 39), np.float32)
     ref_onboard().tb_ref_onboard_batch(_addr(obs), _addr(mission), n, _addr(out))
+    return out
+
+
+def ref_onboard_cr() -> ctypes.CDLL:
+    global _ref_onboard_cr
+    if _ref_onboard_cr is None:
+        if not os.path.exists(REF_ONBOARD_CR_PATH):
+            raise RuntimeError(f"{REF_ONBOARD_CR_PATH} missing (reference build not available)")
+        l = ctypes.CDLL(REF_ONBOARD_CR_PATH)
+        l.tb_ref_onboard_cr_batch.restype = None
+        l.tb_ref_onboard_cr_batch.argtypes = [_vp, _vp, _sz, _vp]
+        _ref_onboard_cr = l
+    return _ref_onboard_cr
+
+
+def onboard_reference_cr(obs, mission):
+    """[n,39] from the reference header with correctly rounded float transcendentals."""
+    n = obs.shape[0]
+    assert obs.dtype == np.float32 and obs.shape == (n, 4148) and obs.flags.c_contiguous
+    assert mission.dtype == np.float32 and mission.shape == (n, 10) and mission.flags.c_contiguous
+    out = np.empty((n, 39), np.float32)
+    ref_onboard_cr().tb_ref_onboard_cr_batch(_addr(obs), _addr(mission), n, _addr(out))
     return out

@@ -76,6 +76,7 @@ def load_library() -> ctypes.CDLL:
     _bind(lib, "tb_cuda_feature_batch_error", _c.c_char_p, [_vp])
     _bind(lib, "tb_cuda_extract_features_host", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
     _bind(lib, "tb_cuda_extract_features_host_noalloc", _c.c_int, [_vp, _vp, _vp, _sz, _vp, _vp])
+    _bind(lib, "tb_cuda_extract_onboard_device", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
     _bind(lib, "tb_features_launch", _c.c_int,
           [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_status_take", _c.c_int, [_vp, _c.POINTER(_c.c_uint)])
@@ -137,6 +138,13 @@ def tb_cuda_extract_features_host(handle: Optional[int], obs, mission, cameras, 
 
 
 # ---- additive entry points ----
+
+def tb_cuda_extract_onboard_device(obs, mission, tactical_24, prior_15, batch_size: int,
+                                   stream=None) -> int:
+    """Onboard tactical [B,24] and prior [B,15] values (device pointers)."""
+    return load_library().tb_cuda_extract_onboard_device(
+        _ptr(obs), _ptr(mission), _ptr(tactical_24), _ptr(prior_15), batch_size, _stream_handle(stream))
+
 
 #: Largest count accepted by tb_cuda_extract_features_host_noalloc (cuda_features.h).
 NOALLOC_MAX_BATCH = 64
