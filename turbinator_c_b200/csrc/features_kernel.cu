@@ -272,7 +272,11 @@ __global__ void __launch_bounds__(kThreads, 2) features_staged_kernel(const Stag
         for (unsigned long long sample = first; sample < a.batch; sample += step, ++k) {
             const int s = static_cast<int>(k % kStages);
             const uint32_t phase = static_cast<uint32_t>((k / kStages) & 1);
-            if (!mbar_wait(empty_bar + 8 * s, phase ^ 1u, a.wait_ns)) { ok = false; break; }
+            /* warp-uniform: every lane leaves together or none does */
+            if (!__all_sync(0xffffffffu, mbar_wait(empty_bar + 8 * s, phase ^ 1u, a.wait_ns))) {
+                ok = false;
+                break;
+            }
             if (static_cast<long long>(sample) == a.stall_sample) continue; /* test hook */
             const uint32_t stage = smem_addr(stages + static_cast<size_t>(s) * kStageBytes);
             if (lane < kMissionDim) {
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 2) features_staged_kernel(const Stag
     for (unsigned long long sample = first; sample < a.batch; sample += step, ++k) {
         const int s = static_cast<int>(k % kStages);
         const uint32_t phase = static_cast<uint32_t>((k / kStages) & 1);
-        if (!mbar_wait(full_bar + 8 * s, phase, a.wait_ns)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(full_bar + 8 * s, phase, a.wait_ns))) {
             if (lane == 0) atomicOr(&g_feature_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
             return;
         }
@@ -565,7 +569,7 @@ extern "C" int tb_cuda_extract_features_device(const float *device_obs, const fl
 
 extern "C" int tb_cuda_synchronize(void *stream) {
     if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return 0;
-    unsigned int status = 0;
-    if (!tb_features_status_take(stream, &status)) return 0;
-    return status == 0;
+    unsigned int features = 0, onboard = 0;
+    if (!tb_features_status_take(stream, &features) || !tb_onboard_status_take(stream, &onboard)) return 0;
+    return (features | onboard) == 0;
 }

@@ -10,15 +10,18 @@
  * Work split (B200):
  *  - The two LiDAR passes over the 1,536 controller rays (2 heads x 6
  *    elevations x 128 azimuths) dominate.  A warp takes one aircraft at a
- *    time and 32 consecutive rays per step (one coalesced 128-byte load);
- *    pass 1's "first strictly smaller" minima (nearest range with its world
- *    offset, nearest obstacle centre) become a warp (value, ray index)
- *    arg-min, and pass 2's cluster count and sum are a ballot + popcount and
- *    an in-order shuffle walk over the ballot, so the float sum keeps the
- *    reference's ray order and rounding.
- *  - The scalar control law then runs one aircraft per lane: a warp owns 32
- *    consecutive aircraft, first sweeps their rays together, then lets each
- *    lane finish its own aircraft.
+ *    time and 32 consecutive rays per step (one coalesced 128-byte load).
+ *    Pass 1 keeps per-lane "first strictly smaller" minima (nearest range
+ *    with its world offset, nearest corridor centre), merged by one warp
+ *    (value, ray index) arg-min at the end, and caches each ray's corridor
+ *    centre in shared memory; pass 2 reads that cache, counts members with
+ *    a ballot + popcount and sums their y with an in-order shuffle walk over
+ *    the ballot, so the float sum keeps the reference's ray order and
+ *    rounding.
+ *  - Only aircraft whose mission reads the scans (dodge, slalom) are
+ *    scanned; a CTA lists them per chunk of 512 aircraft and deals them to
+ *    its warps round-robin.  The scalar control law then runs one aircraft
+ *    per thread.
  *  - Ray directions (12 elevation and 128 azimuth cosines/sines) are built
  *    once per CTA in shared memory.
  *
@@ -43,9 +46,12 @@ namespace {
 constexpr int kObsDim = 4148;
 constexpr int kMissionDim = 10;
 constexpr int kRays = 1536;     /* 2 heads x 6 elevations x 128 azimuths */
-constexpr int kWarps = 8;
+constexpr int kWarps = 11;
+constexpr int kChunk = 512;    /* aircraft per CTA step */
 constexpr int kThreads = 32 * kWarps;
 constexpr unsigned kFull = 0xffffffffu;
+constexpr unsigned long long kWaitNs = 1000000000ull; /* ~1 s limit on each staging wait */
+constexpr uint32_t kHeadBlockBytes = 6 * 128 * 4;      /* elevation rows 0..5 of one head */
 
 /* ---- correctly rounded float transcendentals (double, one rounding) ---- */
 __device__ __forceinline__ float cr_sin(float x) { return static_cast<float>(sin(static_cast<double>(x))); }
@@ -93,7 +99,8 @@ __device__ __forceinline__ float unit_sane(float x) {
 struct RayStats {
     float min_r, min_r_dx, min_r_dy;  /* nearest return in elevations 0..3 and its world x, y */
     float min_dx_c;                   /* nearest obstacle centre ahead inside the corridor */
-    float cluster_y_sum;              /* sum of corridor centres' y within 1.4 m of min_dx_c */
+    float cluster_y_sum;              /* sum of corridor centres' y within 1.4 m of min_dx_c, or a
+                                         value of the same sign (only its sign is read) */
     int cluster_count;
 };
 
@@ -150,38 +157,77 @@ __device__ void build_ray_tables(RayTables &t) {
     }
 }
 
-/* One ray of the controller scan: world offset of the return. */
-struct RayHit {
-    bool valid;   /* 0.35 < range < 11.5 */
-    bool low;     /* elevation index < 4 */
-    float range, wx, wy, x_center, y_center;
-    bool corridor; /* |wz| <= 2.1 and the centre lies in the forward corridor */
+/* Sticky status word of this file's kernels (bit 1: a staging wait expired). */
+__device__ unsigned int g_onboard_status;
+
+/* Per-warp shared memory: a two-deep ring of staged LiDAR blocks (the 1,536
+ * controller rays of one aircraft, in ray order) and pass 1's corridor-centre
+ * x per ray (+inf outside the corridor), which pass 2 reads back. */
+struct WarpSlot {
+    float ranges[2][kRays];
+    float corridor_x[kRays];
+    unsigned long long bar[2];
 };
 
-__device__ __forceinline__ RayHit cast_ray(const RayTables &t, const Attitude &a, float py, int ray,
-                                           float raw_range) {
-    RayHit h;
-    const int row = ray >> 7;          /* head * 6 + el */
-    const int azi = ray & 127;
-    const int el = row % 6;
-    const float range = obs_value(raw_range);
-    h.range = range;
-    h.valid = range > 0.35f && range < 11.5f;
-    h.low = el < 4;
-    const float ce = t.cos_el[row], se = t.sin_el[row];
-    const float rx = ce * t.cos_az[azi], ry = ce * t.sin_az[azi];
-    const float rz = se;
-    const float rwx = a.r00 * rx + a.r01 * ry + a.r02 * rz;
-    const float rwy = a.r10 * rx + a.r11 * ry + a.r12 * rz;
-    const float rwz = a.r20 * rx + a.r21 * ry + a.r22 * rz;
-    h.wx = rwx * range;
-    h.wy = rwy * range;
-    const float wz = rwz * range;
-    h.x_center = h.wx + rwx * 1.10f;
-    h.y_center = py + h.wy + rwy * 1.10f;
-    h.corridor = h.valid && fabsf(wz) <= 2.1f && h.x_center >= -0.35f && h.x_center <= 10.5f &&
-                 fabsf(h.y_center) <= 3.5f;
-    return h;
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+/* Bounded wait (about one second of %globaltimer); false on expiry. */
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    unsigned long long t0, t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+        if (t1 - t0 > kWaitNs) return false;
+    }
+}
+
+/* Stage aircraft `row`'s two LiDAR blocks (heads 0 and 1, elevations 0..5)
+ * into ranges[stage].  16-byte aligned rows take two 1-D bulk copies
+ * completing on bar[stage] (issued by lane 0); other rows are copied by the
+ * warp with plain loads, and bar[stage] is then just arrived on. */
+__device__ __forceinline__ void stage_rays(WarpSlot &slot, int stage, const float *obs_row, bool bulk,
+                                           int lane) {
+    const uint32_t bar = smem_addr(&slot.bar[stage]);
+    float *dst = slot.ranges[stage];
+    if (bulk) {
+        if (lane == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                         "r"(2u * kHeadBlockBytes)
+                         : "memory");
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_addr(dst)),
+                "l"(obs_row + 48), "r"(kHeadBlockBytes), "r"(bar)
+                : "memory");
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_addr(dst + kRays / 2)),
+                "l"(obs_row + 48 + 2048), "r"(kHeadBlockBytes), "r"(bar)
+                : "memory");
+        }
+    } else {
+        for (int i = lane; i < kRays; i += 32) dst[i] = __ldg(obs_row + 48 + (i >= kRays / 2 ? 2048 - kRays / 2 : 0) + i);
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+    }
 }
 
 /* Warp arg-min of (value, index): smallest value, then smallest index. */
@@ -194,63 +240,145 @@ __device__ __forceinline__ void warp_argmin(float &v, int &idx) {
     }
 }
 
-/* Global ray index r (0..1535) -> LiDAR bin offset in the observation. */
-__device__ __forceinline__ int ray_bin(int ray) {
-    const int row = ray >> 7, azi = ray & 127;
-    const int head = row / 6, el = row % 6;
-    return 48 + (head * 16 + el) * 128 + azi;
-}
+/* Both controller LiDAR passes for one staged aircraft, by the whole warp.
+ * Ray r (0..1535) is (head, el, azi) in the reference's loop order; lane l
+ * owns rays with azi % 32 == l and visits them in increasing r, so its
+ * running "strictly smaller" minima keep the first occurrence, and the warp
+ * arg-min by (value, ray) reproduces the sequential result.  A range outside
+ * (0.35, 11.5) never enters either pass, and the observation sanitiser maps
+ * NaN and +-inf outside that window, so raw ranges are used directly.
+ *
+ * The control law reads the nearest return (min_r and its offsets) only for
+ * dodge missions, and the corridor results (min_dx_c, cluster count, cluster
+ * y) only for slalom missions -- and of the cluster y sum only its sign
+ * (onboard_features.cuh:234-239).  `want_near` / `want_corridor`
+ * (warp-uniform) select what is computed; the fields not asked for keep the
+ * reference's initial values.  The sign of the reference's in-order float
+ * sum is decided from a double-precision sum and a bound on the float sum's
+ * rounding error ((n-1) * 2^-24 * sum|y| for n terms, doubled for margin);
+ * only when that bound cannot settle the sign is the exact in-order float
+ * sum formed (an in-order shuffle walk over each chunk's ballot).  Every lane
+ * returns the same RayStats. */
+__device__ RayStats scan_rays(const RayTables &t, WarpSlot &slot, const float *ranges,
+                              const Attitude &a, float py, const float (&cos_az)[4],
+                              const float (&sin_az)[4], int lane, bool want_near, bool want_corridor) {
+    const float inf = __int_as_float(0x7f800000);
+    float near_r = inf, near_wx = 0.0f, near_wy = 0.0f;
+    int near_ray = 0x7fffffff;
+    float ahead_x = inf;
+    int ahead_ray = 0x7fffffff;
 
-/* Both controller LiDAR passes for one aircraft, by the whole warp.  Every
- * lane returns the same RayStats. */
-__device__ RayStats scan_rays(const RayTables &t, const float *obs_row, int lane) {
-    const Attitude a = attitude_from(obs_value(__ldg(obs_row + 6)), obs_value(__ldg(obs_row + 7)),
-                                     obs_value(__ldg(obs_row + 8)), obs_value(__ldg(obs_row + 9)));
-    const float py = obs_value(__ldg(obs_row + 1));
+    /* Pass 1 (onboard_features.cuh:188-207). */
+#pragma unroll 2
+    for (int row = 0; row < 12; ++row) {          /* head * 6 + el */
+        const int el = row >= 6 ? row - 6 : row;
+        const float ce = t.cos_el[row], se = t.sin_el[row];
+        const bool near_row = want_near && el < 4;
+        if (!near_row && !want_corridor) continue;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int ray = row * 128 + q * 32 + lane;
+            const float range = ranges[ray];
+            const bool valid = range > 0.35f && range < 11.5f;
+            const float rx = ce * cos_az[q], ry = ce * sin_az[q];
+            const float rz = se;
+            const float rwx = a.r00 * rx + a.r01 * ry + a.r02 * rz;
+            const float rwy = a.r10 * rx + a.r11 * ry + a.r12 * rz;
+            const float wx = rwx * range, wy = rwy * range;
+            if (near_row && valid && range < near_r) {
+                near_r = range;
+                near_ray = ray;
+                near_wx = wx;
+                near_wy = wy;
+            }
+            if (want_corridor) {
+                const float rwz = a.r20 * rx + a.r21 * ry + a.r22 * rz;
+                const float wz = rwz * range;
+                const float x_center = wx + rwx * 1.10f;
+                const float y_center = py + wy + rwy * 1.10f;
+                const bool corridor = valid && fabsf(wz) <= 2.1f && x_center >= -0.35f &&
+                                      x_center <= 10.5f && fabsf(y_center) <= 3.5f;
+                if (corridor && x_center < ahead_x) {
+                    ahead_x = x_center;
+                    ahead_ray = ray;
+                }
+                slot.corridor_x[ray] = corridor ? x_center : inf;
+            }
+        }
+    }
+
     RayStats s;
     s.min_r = 30.0f;
     s.min_r_dx = 0.0f;
     s.min_r_dy = 0.0f;
     s.min_dx_c = 30.0f;
-
-    /* Pass 1: nearest low-elevation return (first strictly smaller wins) and
-     * nearest corridor centre. */
-    for (int base = 0; base < kRays; base += 32) {
-        const int ray = base + lane;
-        const RayHit h = cast_ray(t, a, py, ray, __ldg(obs_row + ray_bin(ray)));
-        float v = (h.valid && h.low) ? h.range : __int_as_float(0x7f800000);
-        int idx = ray;
-        warp_argmin(v, idx);
-        if (v < s.min_r) {
-            s.min_r = v;
-            s.min_r_dx = __shfl_sync(kFull, h.wx, idx - base);
-            s.min_r_dy = __shfl_sync(kFull, h.wy, idx - base);
+    s.cluster_count = 0;
+    s.cluster_y_sum = 0.0f;
+    if (want_near) {
+        const float lane_wx = near_wx, lane_wy = near_wy;
+        warp_argmin(near_r, near_ray);
+        if (near_r < 30.0f) {
+            s.min_r = near_r;
+            s.min_r_dx = __shfl_sync(kFull, lane_wx, near_ray & 31);
+            s.min_r_dy = __shfl_sync(kFull, lane_wy, near_ray & 31);
         }
-        float c = h.corridor ? h.x_center : __int_as_float(0x7f800000);
-        int cidx = ray;
-        warp_argmin(c, cidx);
-        if (c < s.min_dx_c) s.min_dx_c = c;
     }
+    if (!want_corridor) return s;
+    warp_argmin(ahead_x, ahead_ray);
+    s.min_dx_c = ahead_x < 30.0f ? ahead_x : 30.0f;
+    __syncwarp();
 
-    /* Pass 2: corridor centres within 1.4 m of the nearest; their y summed
-     * in ray order. */
+    /* Pass 2 (onboard_features.cuh:213-233): corridor centres within 1.4 m
+     * of the nearest.  y is recomputed for member rays only. */
     const float limit = s.min_dx_c + 1.4f;
     int count = 0;
-    float ysum = 0.0f;
+    double dsum = 0.0, dabs = 0.0;
+#pragma unroll 4
     for (int base = 0; base < kRays; base += 32) {
         const int ray = base + lane;
-        const RayHit h = cast_ray(t, a, py, ray, __ldg(obs_row + ray_bin(ray)));
-        const bool member = h.corridor && h.x_center <= limit;
-        unsigned mask = __ballot_sync(kFull, member);
-        count += __popc(mask);
-        while (mask) {
-            const int src = __ffs(mask) - 1;
-            ysum += __shfl_sync(kFull, h.y_center, src);
-            mask &= mask - 1;
+        const bool member = slot.corridor_x[ray] <= limit;
+        count += __popc(__ballot_sync(kFull, member));
+        if (member) {
+            const int row = ray >> 7, azi = ray & 127;
+            const float ce = t.cos_el[row];
+            const float rx = ce * t.cos_az[azi], ry = ce * t.sin_az[azi], rz = t.sin_el[row];
+            const float rwy = a.r10 * rx + a.r11 * ry + a.r12 * rz;
+            const float y = py + rwy * ranges[ray] + rwy * 1.10f;
+            dsum += static_cast<double>(y);
+            dabs += fabs(static_cast<double>(y));
         }
     }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        dsum += __shfl_xor_sync(kFull, dsum, off);
+        dabs += __shfl_xor_sync(kFull, dabs, off);
+    }
     s.cluster_count = count;
-    s.cluster_y_sum = ysum;
+    const double bound = 2.0 * static_cast<double>(count) * 0x1.0p-24 * dabs;
+    if (fabs(dsum) > bound) {
+        /* Sign settled: the in-order float sum has the sign of dsum. */
+        s.cluster_y_sum = dsum > 0.0 ? 1.0f : -1.0f;
+    } else {
+        /* Ambiguous sign: form the reference's in-order float sum exactly. */
+        float ysum = 0.0f;
+        for (int base = 0; base < kRays; base += 32) {
+            const int ray = base + lane;
+            unsigned mask = __ballot_sync(kFull, slot.corridor_x[ray] <= limit);
+            if (mask) {
+                const int row = ray >> 7, azi = ray & 127;
+                const float ce = t.cos_el[row];
+                const float rx = ce * t.cos_az[azi], ry = ce * t.sin_az[azi], rz = t.sin_el[row];
+                const float rwy = a.r10 * rx + a.r11 * ry + a.r12 * rz;
+                const float y = py + rwy * ranges[ray] + rwy * 1.10f;
+                do {
+                    ysum += __shfl_sync(kFull, y, __ffs(mask) - 1);
+                    mask &= mask - 1;
+                } while (mask);
+            }
+        }
+        s.cluster_y_sum = ysum;
+    }
+    __syncwarp();
     return s;
 }
 
@@ -702,53 +830,144 @@ __device__ void prior(const float *o, const float *m, const RayStats &rs, float 
 }
 
 /* ------------------------------------------------------------------ */
-/* One warp per 32 consecutive aircraft: shared ray sweeps, then one lane
- * per aircraft for the control law. */
+/* Persistent: one CTA per SM; each CTA owns a balanced contiguous range of
+ * aircraft and walks it kChunk at a time.  Per chunk: (1) the aircraft whose
+ * mission reads the LiDAR scans (dodge: nearest return; slalom: corridor)
+ * are listed in shared memory; (2) the warps take those scan jobs
+ * round-robin, each staging the next job's LiDAR block with bulk copies
+ * while it scans the current one, and leave the results in shared memory;
+ * (3) every thread runs the control law for one aircraft at a time. */
+struct ChunkState {
+    RayStats stats[kChunk];
+    unsigned short jobs[kChunk];   /* aircraft index in chunk | 0x4000 near | 0x8000 corridor */
+    int job_count;
+};
+
 __global__ void __launch_bounds__(kThreads) onboard_kernel(const float *__restrict__ obs,
                                                            const float *__restrict__ mission,
                                                            float *__restrict__ tactical_out,
                                                            float *__restrict__ prior_out,
                                                            unsigned long long batch) {
     __shared__ RayTables tables;
+    extern __shared__ __align__(128) unsigned char dyn[];
     build_ray_tables(tables);
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    WarpSlot &slot = reinterpret_cast<WarpSlot *>(dyn)[warp];
+    ChunkState &chunk = *reinterpret_cast<ChunkState *>(dyn + sizeof(WarpSlot) * kWarps);
+    if (lane == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&slot.bar[0])) : "memory");
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&slot.bar[1])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     __syncthreads();
 
-    const int lane = threadIdx.x & 31;
-    const unsigned long long groups = (batch + 31) / 32;
-    const unsigned long long warp_global = (static_cast<unsigned long long>(blockIdx.x) * kThreads +
-                                            threadIdx.x) >> 5;
-    const unsigned long long warp_count = (static_cast<unsigned long long>(gridDim.x) * kThreads) >> 5;
+    float cos_az[4], sin_az[4];
+    for (int q = 0; q < 4; ++q) {
+        cos_az[q] = tables.cos_az[q * 32 + lane];
+        sin_az[q] = tables.sin_az[q * 32 + lane];
+    }
+    const bool bulk = (reinterpret_cast<uintptr_t>(obs) & 15) == 0;
+    const unsigned long long begin = batch * blockIdx.x / gridDim.x;
+    const unsigned long long end = batch * (blockIdx.x + 1) / gridDim.x;
+    uint32_t seq = 0;            /* LiDAR blocks staged by this warp so far */
+    bool failed = false;
 
-    for (unsigned long long g = warp_global; g < groups; g += warp_count) {
-        const unsigned long long first = g * 32;
-        const int members = static_cast<int>(batch - first < 32 ? batch - first : 32);
-        RayStats mine{};
-        for (int k = 0; k < members; ++k) {
-            const RayStats s = scan_rays(tables, obs + (first + k) * kObsDim, lane);
-            if (k == lane) mine = s;
+    for (unsigned long long first = begin; first < end; first += kChunk) {
+        const int n = static_cast<int>(end - first < kChunk ? end - first : kChunk);
+        if (threadIdx.x == 0) chunk.job_count = 0;
+        __syncthreads();
+        /* (1) scan jobs of this chunk */
+        for (int i = threadIdx.x; i < n; i += kThreads) {
+            RayStats &st = chunk.stats[i];
+            st.min_r = 30.0f;
+            st.min_r_dx = 0.0f;
+            st.min_r_dy = 0.0f;
+            st.min_dx_c = 30.0f;
+            st.cluster_y_sum = 0.0f;
+            st.cluster_count = 0;
+            const float m4 = mission_value(__ldg(mission + (first + i) * kMissionDim + 4));
+            const float m5 = mission_value(__ldg(mission + (first + i) * kMissionDim + 5));
+            const bool dodge = m5 > 0.75f;
+            const bool slalom = m4 > 0.75f && !(m4 > 0.75f && m5 > 0.25f);
+            if (dodge || slalom)
+                chunk.jobs[atomicAdd(&chunk.job_count, 1)] =
+                    static_cast<unsigned short>(i | (dodge ? 0x4000 : 0) | (slalom ? 0x8000 : 0));
         }
-        if (lane >= members) continue;
-        const unsigned long long sample = first + lane;
-        const float *row = obs + sample * kObsDim;
-        const float *mrow = mission + sample * kMissionDim;
-        float raw_o[48], raw_m[10], o[48], m[10];
-        for (int i = 0; i < 48; ++i) {
-            raw_o[i] = __ldg(row + i);
-            o[i] = obs_value(raw_o[i]);
+        __syncthreads();
+        /* (2) scan jobs, round-robin over warps */
+        const int jobs = chunk.job_count;
+        int j = warp;
+        if (!failed && j < jobs)
+            stage_rays(slot, seq & 1, obs + (first + (chunk.jobs[j] & 0x3fff)) * kObsDim, bulk, lane);
+        for (; !failed && j < jobs; j += kWarps) {
+            const int job = chunk.jobs[j];
+            const int i = job & 0x3fff;
+            const bool more = j + kWarps < jobs;
+            if (more)
+                stage_rays(slot, (seq + 1) & 1, obs + (first + (chunk.jobs[j + kWarps] & 0x3fff)) * kObsDim,
+                           bulk, lane);
+            /* all lanes take the same branch, even if the copy lands at the deadline */
+            if (!__all_sync(kFull, mbar_wait(smem_addr(&slot.bar[seq & 1]), (seq >> 1) & 1))) {
+                if (lane == 0) atomicOr(&g_onboard_status, 1u);
+                /* no copy may still be in flight into this warp's shared memory */
+                if (more) mbar_wait(smem_addr(&slot.bar[(seq + 1) & 1]), ((seq + 1) >> 1) & 1);
+                failed = true;
+                break;
+            }
+            const float *row = obs + (first + i) * kObsDim;
+            const Attitude a = attitude_from(obs_value(__ldg(row + 6)), obs_value(__ldg(row + 7)),
+                                             obs_value(__ldg(row + 8)), obs_value(__ldg(row + 9)));
+            const RayStats st = scan_rays(tables, slot, slot.ranges[seq & 1], a, obs_value(__ldg(row + 1)),
+                                          cos_az, sin_az, lane, (job & 0x4000) != 0, (job & 0x8000) != 0);
+            if (lane == 0) chunk.stats[i] = st;
+            ++seq;
         }
-        for (int i = 0; i < 10; ++i) {
-            raw_m[i] = __ldg(mrow + i);
-            m[i] = mission_value(raw_m[i]);
+        __syncthreads();
+        /* (3) control law, one aircraft per thread */
+        for (int i = threadIdx.x; i < n; i += kThreads) {
+            const unsigned long long sample = first + i;
+            const float *row = obs + sample * kObsDim;
+            const float *mrow = mission + sample * kMissionDim;
+            float raw_o[48], raw_m[10], o[48], m[10];
+            for (int k = 0; k < 48; ++k) {
+                raw_o[k] = __ldg(row + k);
+                o[k] = obs_value(raw_o[k]);
+            }
+            for (int k = 0; k < 10; ++k) {
+                raw_m[k] = __ldg(mrow + k);
+                m[k] = mission_value(raw_m[k]);
+            }
+            tactical(raw_o, raw_m, tactical_out + sample * 24);
+            prior(o, m, chunk.stats[i], prior_out + sample * 15);
         }
-        tactical(raw_o, raw_m, tactical_out + sample * 24);
-        prior(o, m, mine, prior_out + sample * 15);
+        __syncthreads();
     }
 }
 
 constexpr int kMaxDevices = 64;
+constexpr size_t kDynSmem = sizeof(WarpSlot) * kWarps + sizeof(ChunkState); /* about 211 KiB */
 int g_sms[kMaxDevices];
 
 } /* namespace */
+
+extern "C" int tb_onboard_status_take(void *stream, unsigned int *status) {
+    unsigned int value = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyFromSymbolAsync(&value, g_onboard_status, sizeof(value), 0, cudaMemcpyDeviceToHost, s) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return 0;
+    if (value) {
+        static const unsigned int zero = 0;
+        if (cudaMemcpyToSymbolAsync(g_onboard_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess)
+            return 0;
+    }
+    if (status) *status = value;
+    return 1;
+}
 
 extern "C" int tb_cuda_extract_onboard_device(const float *device_obs, const float *device_mission,
                                               float *device_tactical_24, float *device_prior_15,
@@ -766,14 +985,16 @@ extern "C" int tb_cuda_extract_onboard_device(const float *device_obs, const flo
     if (!g_sms[dev]) {
         int sms = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+        if (cudaFuncSetAttribute(onboard_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kDynSmem)) != cudaSuccess)
+            return 0;
         g_sms[dev] = sms;
     }
     cudaGetLastError(); /* report this launch only */
-    const unsigned long long groups = (batch_size + 31) / 32;
-    unsigned long long grid = (groups + kWarps - 1) / kWarps;
-    const unsigned long long cap = static_cast<unsigned long long>(g_sms[dev]) * 8;
-    if (grid > cap) grid = cap;
-    onboard_kernel<<<static_cast<unsigned int>(grid), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+    /* one CTA per SM (shared memory admits one) */
+    unsigned long long grid = static_cast<unsigned long long>(g_sms[dev]);
+    if (grid > batch_size) grid = batch_size;
+    onboard_kernel<<<static_cast<unsigned int>(grid), kThreads, kDynSmem, static_cast<cudaStream_t>(stream)>>>(
         device_obs, device_mission, device_tactical_24, device_prior_15, batch_size);
     return cudaGetLastError() == cudaSuccess;
 }

@@ -47,6 +47,9 @@ int tb_features_launch_checked(const float *obs, const float *mission,
  * Returns 1 if the read succeeded; *status receives the bits. */
 int tb_features_status_take(void *stream, unsigned int *status);
 
+/* As tb_features_status_take, for the onboard kernel's own status word. */
+int tb_onboard_status_take(void *stream, unsigned int *status);
+
 /* Launch geometry of the staged kernel on the current device. */
 int tb_features_staged_config(int *blocks_per_sm, int *sms, int *smem_bytes, int *threads,
                               int *stages);
