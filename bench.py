@@ -58,6 +58,7 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=0, help="host-ABI steps (default: --steps, max 20)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=4.0, help="target wall time of the CPU sample")
+    p.add_argument("--no-onboard", action="store_true", help="skip the onboard tactical/prior leg")
     return p.parse_args()
 
 
@@ -192,6 +193,66 @@ def time_reference_cpu(obs, mission, cams, target_s: float):
                       f"over contiguous ranges, {spent:.2f} s wall; host CPU: {cpu_description()}"}
 
 
+def scanning_fraction(mission) -> float:
+    """Share of aircraft whose mission reads the onboard LiDAR scans (dodge:
+    mission[5] > 0.75; slalom: mission[4] > 0.75 and mission[5] <= 0.25)."""
+    m = np.nan_to_num(np.asarray(mission, np.float32), nan=0.0, posinf=1.0, neginf=-1.0)
+    dodge = m[:, 5] > 0.75
+    slalom = (m[:, 4] > 0.75) & ~(m[:, 5] > 0.25)
+    return float(np.mean(dodge | slalom))
+
+
+def onboard_bytes_per_aircraft(frac_scan: float) -> float:
+    """Algorithmic bytes of the onboard path: observation head (192 B) and
+    mission (40 B) read, 156 B written, plus the two 3,072 B LiDAR blocks of
+    aircraft that scan."""
+    return 192 + 40 + 156 + frac_scan * 2 * 3072
+
+
+def all_scanning(mission):
+    m = np.array(mission, copy=True)
+    m[0::2, 5] = 1.0            # dodge
+    m[1::2, 4] = 1.0            # slalom
+    m[1::2, 5] = -0.5
+    return m
+
+
+def time_onboard(d_obs, mission_host, count, steps, warmup, stream, dev):
+    import torch
+
+    d_mis = torch.from_numpy(np.ascontiguousarray(mission_host)).to(dev)
+    tac = torch.empty((count, 24), dtype=torch.float32, device=dev)
+    pri = torch.empty((count, 15), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize(dev)
+    for _ in range(max(warmup, 3)):
+        assert tb.tb_cuda_extract_onboard_device(d_obs, d_mis, tac, pri, count, stream) == 1
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        tb.tb_cuda_extract_onboard_device(d_obs, d_mis, tac, pri, count, stream)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    if tb.tb_cuda_synchronize(stream.cuda_stream) != 1:
+        raise RuntimeError("onboard kernel reported a pipeline timeout")
+    return start.elapsed_time(end) / 1e3 / steps
+
+
+def time_onboard_reference_cpu(obs, mission, target_s: float):
+    import oracle  # test infrastructure: the CPU baseline only
+
+    threads = host_threads()
+    n = obs.shape[0]
+    out = np.empty((n, 39), np.float32)
+    probe = min(n, max(threads * 16, 1024))
+    rate = probe / max(oracle.timed_onboard_reference(obs[:probe], mission[:probe], out[:probe], threads), 1e-9)
+    sample = int(min(n, max(probe, rate * target_s)))
+    t = oracle.timed_onboard_reference(obs[:sample], mission[:sample], out[:sample], threads)
+    return {"value": sample / t, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"first {sample} aircraft, reference onboard header (glibc build), {threads} threads, "
+                      f"{t:.2f} s wall"}
+
+
 # ---------------------------------------------------------------- arms
 
 def run_reference_arm(args, rank: int, world: int):
@@ -290,6 +351,23 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     kernel_s_max = max_over_ranks(kernel_s)
     value = total * args.steps / kernel_s_max
 
+    # ---- secondary path: onboard tactical/prior values on the same resident inputs
+    onboard = None
+    if not args.no_onboard:
+        legs = {}
+        for name, mis_host in (("mission_mix", mission), ("all_scanning", all_scanning(mission))):
+            per_launch = time_onboard(d_obs, mis_host, count, args.steps, args.warmup, stream, dev)
+            per_launch_max = max_over_ranks(per_launch)
+            frac = scanning_fraction(mis_host)
+            bpa = onboard_bytes_per_aircraft(frac)
+            legs[name] = {"value": total / per_launch_max, "unit": UNIT,
+                          "ms_per_launch": per_launch_max * 1e3, "scanning_fraction": frac,
+                          "algorithmic_bytes_per_aircraft": bpa,
+                          "achieved_gbs": count * bpa / per_launch / 1e9}
+        onboard = {"entry_point": "tb_cuda_extract_onboard_device", "outputs": "24 tactical + 15 prior",
+                   "bound": "SM instruction issue (control law + LiDAR scans), not HBM", **legs,
+                   "launches": 2 * args.steps}
+
     # ---- e2e: the reference-facing host ABI on page-locked host buffers
     e2e_steps = args.e2e_steps or min(args.steps, 20)
     out_host = torch.empty((count, 142), dtype=torch.float32, pin_memory=True).numpy()
@@ -349,12 +427,17 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                      "traffic": (tps * count) if tps else None,
                      "algorithmic_bytes_per_launch": count * tb.BYTES_PER_SAMPLE,
                      "kernel": "features_staged_kernel", "avg_launch_ms": avg_launch_s * 1e3},
-        "gpu_launches": args.steps + e2e_steps * chunks,
-        "gpu_launches_detail": {"value_region": args.steps, "e2e_region": e2e_steps * chunks},
+        "gpu_launches": args.steps + e2e_steps * chunks + (onboard["launches"] if onboard else 0),
+        "gpu_launches_detail": {"value_region": args.steps, "e2e_region": e2e_steps * chunks,
+                                "onboard_regions": onboard["launches"] if onboard else 0},
         "clocks": clk,
     }
+    if onboard is not None:
+        line["onboard"] = onboard
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = time_reference_cpu(obs, mission, cams, args.cpu_seconds)
+        if onboard is not None:
+            onboard["cpu_baseline"] = time_onboard_reference_cpu(obs, mission, args.cpu_seconds / 2)
     print(json.dumps(line), flush=True)
 
 

@@ -45,6 +45,8 @@ def lib() -> ctypes.CDLL:
         l.oracle_extract_features.argtypes = [_vp, _vp, _vp, _vp]
         l.oracle_extract_batch.restype = ctypes.c_double
         l.oracle_extract_batch.argtypes = [_vp, _vp, _vp, _vp, _sz, _vp, ctypes.c_int]
+        l.oracle_onboard_batch.restype = ctypes.c_double
+        l.oracle_onboard_batch.argtypes = [_vp, _vp, _vp, _sz, _vp, ctypes.c_int]
         l.oracle_extract_batch_self.restype = ctypes.c_double
         l.oracle_extract_batch_self.argtypes = [_vp, _vp, _vp, _sz, _vp, ctypes.c_int]
         _oracle = l
@@ -75,6 +77,8 @@ def ref_onboard() -> ctypes.CDLL:
         l = ctypes.CDLL(REF_ONBOARD_PATH)
         l.tb_ref_onboard_batch.restype = None
         l.tb_ref_onboard_batch.argtypes = [_vp, _vp, _sz, _vp]
+        l.tb_ref_onboard_tactical_prior.restype = None
+        l.tb_ref_onboard_tactical_prior.argtypes = [_vp, _vp, _vp, _vp]
         _ref_onboard = l
     return _ref_onboard
 
@@ -154,3 +158,15 @@ def onboard_reference_cr(obs, mission):
     out = np.empty((n, 39), np.float32)
     ref_onboard_cr().tb_ref_onboard_cr_batch(_addr(obs), _addr(mission), n, _addr(out))
     return out
+
+
+def timed_onboard_reference(obs, mission, out, threads: int) -> float:
+    """Wall seconds for the reference onboard header (glibc build) over the
+    batch on `threads` host threads; fills out [n,39]."""
+    n = obs.shape[0]
+    assert obs.flags.c_contiguous and mission.flags.c_contiguous and out.shape == (n, 39)
+    fn = ctypes.cast(ref_onboard().tb_ref_onboard_tactical_prior, _vp).value
+    t = lib().oracle_onboard_batch(fn, _addr(obs), _addr(mission), n, _addr(out), threads)
+    if t < 0:
+        raise RuntimeError("oracle onboard runner failed")
+    return t

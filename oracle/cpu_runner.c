@@ -69,3 +69,43 @@ double oracle_extract_batch_self(const float *obs, const float *mission,
     return oracle_extract_batch(oracle_extract_features, obs, mission, cameras, count, out,
                                 threads);
 }
+
+typedef struct {
+    oracle_onboard_fn fn;
+    const float *obs, *mission;
+    float *out;
+    size_t begin, end;
+} onboard_range;
+
+static void *onboard_range_main(void *arg) {
+    const onboard_range *r = (const onboard_range *)arg;
+    for (size_t i = r->begin; i < r->end; ++i)
+        r->fn(r->obs + i * ORACLE_OBS_DIM, r->mission + i * ORACLE_MISSION_DIM, r->out + i * 39,
+              r->out + i * 39 + 24);
+    return NULL;
+}
+
+double oracle_onboard_batch(oracle_onboard_fn fn, const float *obs, const float *mission,
+                            size_t count, float *out_39, int threads) {
+    if (!fn || !obs || !mission || !out_39) return -1.0;
+    if (threads < 1) threads = 1;
+    if ((size_t)threads > count && count > 0) threads = (int)count;
+    onboard_range *ranges = (onboard_range *)calloc((size_t)threads, sizeof(*ranges));
+    pthread_t *tids = (pthread_t *)calloc((size_t)threads, sizeof(*tids));
+    if (!ranges || !tids) { free(ranges); free(tids); return -1.0; }
+    const double t0 = oracle_now();
+    int started = 0, failed = 0;
+    for (int t = 0; t < threads; ++t) {
+        ranges[t] = (onboard_range){fn, obs, mission, out_39, count * (size_t)t / (size_t)threads,
+                                    count * (size_t)(t + 1) / (size_t)threads};
+        if (t == threads - 1) break;
+        if (pthread_create(&tids[t], NULL, onboard_range_main, &ranges[t]) != 0) { failed = 1; break; }
+        ++started;
+    }
+    if (!failed) onboard_range_main(&ranges[threads - 1]);
+    for (int t = 0; t < started; ++t) pthread_join(tids[t], NULL);
+    const double elapsed = oracle_now() - t0;
+    free(ranges);
+    free(tids);
+    return failed ? -1.0 : elapsed;
+}

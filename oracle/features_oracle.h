@@ -41,6 +41,16 @@ double oracle_extract_batch_self(const float *obs, const float *mission,
                                  const uint8_t *cameras, size_t count, float *out,
                                  int threads);
 
+/* Per-aircraft onboard tactical(24)/prior(15) signature of the reference
+ * header built for the host (oracle/_ref, tb_ref_onboard_tactical_prior). */
+typedef void (*oracle_onboard_fn)(const float *, const float *, float *, float *);
+
+/* Runs `fn` over [count,4148]/[count,10] rows with `threads` POSIX threads,
+ * writing [count,39] (24 tactical then 15 prior).  Returns wall seconds or a
+ * negative value on failure. */
+double oracle_onboard_batch(oracle_onboard_fn fn, const float *obs, const float *mission,
+                            size_t count, float *out_39, int threads);
+
 #ifdef __cplusplus
 }
 #endif
