@@ -59,6 +59,7 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=4.0, help="target wall time of the CPU sample")
     p.add_argument("--no-onboard", action="store_true", help="skip the onboard tactical/prior leg")
+    p.add_argument("--no-f32cam", action="store_true", help="skip the FP32-camera entry-point leg")
     return p.parse_args()
 
 
@@ -351,6 +352,37 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     kernel_s_max = max_over_ranks(kernel_s)
     value = total * args.steps / kernel_s_max
 
+    # ---- FP32-camera entry point (BASELINE's byte sizes): same rows, float cameras
+    f32cam = None
+    if not args.no_f32cam:
+        _, _, _, camf = tb.generate(SEED, first, count, total=total, threads=gen_threads, f32_cameras=True)
+        d_camf = torch.from_numpy(camf).to(dev)
+        del camf
+        for _ in range(max(args.warmup, 3)):
+            assert tb.tb_cuda_extract_features_device_f32cam(d_obs, d_mis, d_camf, d_out, count, stream) == 1
+        torch.cuda.synchronize(dev)
+        barrier()
+        f_start, f_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f_start.record(stream)
+        for _ in range(args.steps):
+            tb.tb_cuda_extract_features_device_f32cam(d_obs, d_mis, d_camf, d_out, count, stream)
+        f_end.record(stream)
+        torch.cuda.synchronize(dev)
+        if tb.tb_cuda_synchronize(stream.cuda_stream) != 1:
+            raise RuntimeError("FP32-camera kernel reported a pipeline timeout")
+        f_per = f_start.elapsed_time(f_end) / 1e3 / args.steps
+        f_per_max = max_over_ranks(f_per)
+        peak_gbs, _ = measured_hbm_peak()
+        f_ach = count * tb.BYTES_PER_SAMPLE_F32CAM / f_per / 1e9
+        f32cam = {"entry_point": "tb_cuda_extract_features_device_f32cam",
+                  "value": total / f_per_max, "unit": UNIT, "ms_per_launch": f_per_max * 1e3,
+                  "bytes_per_sample": tb.BYTES_PER_SAMPLE_F32CAM,
+                  "roofline": {"bound": "hbm", "achieved": f_ach, "peak": peak_gbs, "unit": "GB/s",
+                               "frac": f_ach / peak_gbs},
+                  "launches": args.steps}
+        del d_camf
+        torch.cuda.empty_cache()
+
     # ---- secondary path: onboard tactical/prior values on the same resident inputs
     onboard = None
     if not args.no_onboard:
@@ -427,11 +459,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                      "traffic": (tps * count) if tps else None,
                      "algorithmic_bytes_per_launch": count * tb.BYTES_PER_SAMPLE,
                      "kernel": "features_staged_kernel", "avg_launch_ms": avg_launch_s * 1e3},
-        "gpu_launches": args.steps + e2e_steps * chunks + (onboard["launches"] if onboard else 0),
+        "gpu_launches": (args.steps + e2e_steps * chunks + (onboard["launches"] if onboard else 0) +
+                         (f32cam["launches"] if f32cam else 0)),
         "gpu_launches_detail": {"value_region": args.steps, "e2e_region": e2e_steps * chunks,
-                                "onboard_regions": onboard["launches"] if onboard else 0},
+                                "onboard_regions": onboard["launches"] if onboard else 0,
+                                "f32cam_region": f32cam["launches"] if f32cam else 0},
         "clocks": clk,
     }
+    if f32cam is not None:
+        line["f32_cameras"] = f32cam
     if onboard is not None:
         line["onboard"] = onboard
     if world == 1 and not args.no_cpu_baseline:

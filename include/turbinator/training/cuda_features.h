@@ -96,6 +96,21 @@ int tb_cuda_extract_onboard_device(const float *device_obs,
                                    size_t batch_size,
                                    void *stream);
 
+/* FP32-camera variant of tb_cuda_extract_features_device (no counterpart in
+ * the reference, whose ABI takes u8 cameras).  device_cameras_f32 is
+ * [batch, 4*64*64] float luma, nominally in [0, 1]; each value is quantised
+ * on load exactly as the simulator quantises luma for the u8 ABI
+ * (src/sim/sensors.c:67: fmax(0, fmin(255, round(v * 255))) in double, so
+ * NaN reads as 255), so the features equal those of
+ * tb_cuda_extract_features_device on the quantised bytes.  May be NULL
+ * (camera features 0).  Same return values and stream semantics. */
+int tb_cuda_extract_features_device_f32cam(const float *device_obs,
+                                           const float *device_mission,
+                                           const float *device_cameras_f32,
+                                           float *device_features,
+                                           size_t batch_size,
+                                           void *stream);
+
 /* Largest count accepted by tb_cuda_extract_features_host_noalloc. */
 #define TB_CUDA_NOALLOC_MAX_BATCH 64
 

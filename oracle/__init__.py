@@ -45,6 +45,8 @@ def lib() -> ctypes.CDLL:
         l.oracle_extract_features.argtypes = [_vp, _vp, _vp, _vp]
         l.oracle_extract_batch.restype = ctypes.c_double
         l.oracle_extract_batch.argtypes = [_vp, _vp, _vp, _vp, _sz, _vp, ctypes.c_int]
+        l.oracle_quantize_cameras.restype = None
+        l.oracle_quantize_cameras.argtypes = [_vp, _sz, _vp]
         l.oracle_onboard_batch.restype = ctypes.c_double
         l.oracle_onboard_batch.argtypes = [_vp, _vp, _vp, _sz, _vp, ctypes.c_int]
         l.oracle_extract_batch_self.restype = ctypes.c_double
@@ -170,3 +172,11 @@ def timed_onboard_reference(obs, mission, out, threads: int) -> float:
     if t < 0:
         raise RuntimeError("oracle onboard runner failed")
     return t
+
+
+def quantize_cameras(cameras_f32):
+    """u8 cameras from float luma with the simulator's rule (sensors.c:67)."""
+    c = np.ascontiguousarray(cameras_f32, np.float32)
+    out = np.empty(c.shape, np.uint8)
+    lib().oracle_quantize_cameras(_addr(c), c.size, _addr(out))
+    return out

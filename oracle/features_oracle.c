@@ -110,3 +110,15 @@ void oracle_extract_features(const float *obs, const float *mission,
         out[126 + q] = (float)sum / (1024.0f * 255.0f);
     }
 }
+
+/* The simulator's luma quantisation (reference src/sim/sensors.c:67, with
+ * tb_clamp = fmax(lo, fmin(hi, v)) from src/sim/sim_internal.h:73), applied
+ * to one float camera value in double arithmetic.  fmin returns the non-NaN
+ * operand, so NaN quantises to 255. */
+uint8_t oracle_quantize_luma(float v) {
+    return (uint8_t)fmax(0.0, fmin(255.0, round((double)v * 255.0)));
+}
+
+void oracle_quantize_cameras(const float *cameras_f32, size_t count, uint8_t *out) {
+    for (size_t i = 0; i < count; ++i) out[i] = oracle_quantize_luma(cameras_f32[i]);
+}

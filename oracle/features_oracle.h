@@ -25,6 +25,12 @@ enum {
 void oracle_extract_features(const float *obs, const float *mission,
                              const uint8_t *cameras, float *out);
 
+/* The simulator's camera quantisation of float luma values (sensors.c:67):
+ * the oracle for the FP32-camera entry point quantises with this and then
+ * runs the 142-feature path on the bytes.  count is a number of values. */
+uint8_t oracle_quantize_luma(float v);
+void oracle_quantize_cameras(const float *cameras_f32, size_t count, uint8_t *out);
+
 /* Per-sample extractor signature shared by the oracle above and the
  * reference's own tb_train_extract_features_cpu (loaded from oracle/_ref). */
 typedef void (*oracle_sample_fn)(const float *, const float *, const uint8_t *, float *);

@@ -25,7 +25,8 @@ def test_value_model():
     for block in (obs[:, :48], obs[:, 4144:], mission):
         assert np.all(np.abs(block) <= 1.0)
     assert np.all((camf >= 0) & (camf <= 1))
-    q = np.floor(np.clip(camf, 0, 1) * np.float32(255) + np.float32(0.5)).astype(np.uint8)
+    # the simulator's rule (sensors.c:67): round-half-away of v*255 in double
+    q = np.floor(camf.astype(np.float64) * 255.0 + 0.5).astype(np.uint8)
     assert np.array_equal(q, cams)
     rows = camf.reshape(-1, 4, 64, 64).mean(axis=(0, 1, 3))
     assert abs(rows[0] - 0.8) < 0.01 and abs(rows[63] - 0.2) < 0.01

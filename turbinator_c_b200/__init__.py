@@ -29,6 +29,8 @@ ONBOARD_DIM = 39
 #: Algorithmic HBM bytes per aircraft for the u8-camera entry point
 #: (16,592 obs + 40 mission + 16,384 cameras read, 568 features written).
 BYTES_PER_SAMPLE = OBS_DIM * 4 + MISSION_DIM * 4 + CAMERA_BYTES + FEATURE_DIM * 4
+#: The same for the FP32-camera entry point (65,536 camera bytes read).
+BYTES_PER_SAMPLE_F32CAM = OBS_DIM * 4 + MISSION_DIM * 4 + 4 * CAMERA_BYTES + FEATURE_DIM * 4
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libturbinator_cuda.so")
@@ -77,6 +79,9 @@ def load_library() -> ctypes.CDLL:
     _bind(lib, "tb_cuda_extract_features_host", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
     _bind(lib, "tb_cuda_extract_features_host_noalloc", _c.c_int, [_vp, _vp, _vp, _sz, _vp, _vp])
     _bind(lib, "tb_cuda_extract_onboard_device", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
+    _bind(lib, "tb_cuda_extract_features_device_f32cam", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
+    _bind(lib, "tb_features_launch_f32cam", _c.c_int,
+          [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_launch", _c.c_int,
           [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_status_take", _c.c_int, [_vp, _c.POINTER(_c.c_uint)])
@@ -138,6 +143,21 @@ def tb_cuda_extract_features_host(handle: Optional[int], obs, mission, cameras, 
 
 
 # ---- additive entry points ----
+
+def tb_cuda_extract_features_device_f32cam(obs, mission, cameras_f32, features, batch_size: int,
+                                           stream=None) -> int:
+    """142 features from FP32 cameras [B,16384] quantised like the simulator."""
+    return load_library().tb_cuda_extract_features_device_f32cam(
+        _ptr(obs), _ptr(mission), _ptr(cameras_f32), _ptr(features), batch_size, _stream_handle(stream))
+
+
+def launch_f32cam(obs, mission, cameras_f32, features, batch_size: int, stream=None, *,
+                  force_direct: bool = False, grid_limit: int = 0) -> int:
+    opts = LaunchOpts(int(force_direct), int(grid_limit), 0, -1)
+    return load_library().tb_features_launch_f32cam(
+        _ptr(obs), _ptr(mission), _ptr(cameras_f32), _ptr(features), batch_size,
+        _stream_handle(stream), _c.byref(opts))
+
 
 def tb_cuda_extract_onboard_device(obs, mission, tactical_24, prior_15, batch_size: int,
                                    stream=None) -> int:

@@ -59,17 +59,27 @@ constexpr int kLidarOffset = 48;
 constexpr int kTailOffset = 4144;
 
 constexpr uint32_t kObsBytes = kObsDim * 4u;                  /* 16,592 = 16 * 1,037 */
-constexpr uint32_t kStageCamOff = kObsBytes;                  /* 16-byte aligned */
-constexpr uint32_t kStageMissionOff = kStageCamOff + kCameraBytes; /* 32,976 */
-constexpr uint32_t kStageBytes = 33024;                       /* 258 * 128 */
-static_assert(kStageMissionOff + kMissionDim * 4 <= kStageBytes, "stage layout");
 static_assert(kObsBytes % 16 == 0 && kCameraBytes % 16 == 0, "bulk copy sizes");
 
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);
-constexpr int kStages = 3;
 constexpr uint32_t kBarrierRegion = 128;
-constexpr uint32_t kSmemBytes = kBarrierRegion + kStages * kStageBytes;
+
+/* Shared-memory ring geometry per camera format.  A stage holds one
+ * aircraft: observation row, camera block, mission row.  u8 cameras: 33 KB
+ * stages, 3 per CTA, 2 CTAs per SM; FP32 cameras: 82 KB stages, 2 per CTA,
+ * 1 CTA per SM.  Either way ~160-200 KB per SM are in flight. */
+template <bool kF32Cam>
+struct Ring {
+    static constexpr uint32_t camera_bytes = kF32Cam ? 4u * kCameraBytes : kCameraBytes;
+    static constexpr uint32_t cam_off = kObsBytes;
+    static constexpr uint32_t mission_off = cam_off + camera_bytes;
+    static constexpr uint32_t stage_bytes = (mission_off + kMissionDim * 4 + 127) / 128 * 128;
+    static constexpr int stages = kF32Cam ? 2 : 3;
+    static constexpr int min_blocks = kF32Cam ? 1 : 2;
+    static constexpr uint32_t smem_bytes = kBarrierRegion + stages * stage_bytes;
+};
+static_assert(Ring<false>::stage_bytes == 33024 && Ring<true>::stage_bytes == 82176, "stage layout");
 
 /* 1 / log2(121): a LiDAR term log1p(x)/log1p(120) equals log2(1+x) times this. */
 constexpr float kInvLog2_121 = 0.14453241315894394f;
@@ -229,30 +239,55 @@ __device__ __forceinline__ uint32_t byte_sum4(uint32_t w, uint32_t acc) {
     return __dp4a(w, 0x01010101u, acc);
 }
 
+/* The simulator's camera quantisation (reference src/sim/sensors.c:67 with
+ * the clamp of src/sim/sim_internal.h:73): fmax(0, fmin(255, round(v*255)))
+ * in double, so NaN gives 255.  Evaluated exactly in float, as a float byte
+ * value: NaN is tested explicitly (a fused clamp would send it to 0);
+ * clamping other values to [0, 1] first gives the same byte; v*255 is formed
+ * as hi + lo with lo the exact FMA residual, and round-half-away of hi is
+ * taken one lower when hi landed on a half-integer from below (lo < 0).  No
+ * other case can straddle a rounding boundary, because half-integers below
+ * 256 are themselves floats. */
+__device__ __forceinline__ float luma_byte(float v) {
+    const float c = fmaxf(fminf(v, 1.0f), 0.0f);
+    const float hi = __fmul_rn(c, 255.0f);
+    const float lo = __fmaf_rn(c, 255.0f, -hi);
+    const float r = roundf(hi);
+    const float q = (r - hi == 0.5f && lo < 0.0f) ? r - 1.0f : r;
+    return v != v ? 255.0f : q;
+}
+
+__device__ __forceinline__ float luma_bytes4(const float4 v) {
+    return (luma_byte(v.x) + luma_byte(v.y)) + (luma_byte(v.z) + luma_byte(v.w));
+}
+
 /* ------------------------------------------------------------------ */
 /* Staged kernel: persistent, warp-specialised, bulk-copy pipeline. */
 
 struct StagedArgs {
     const float *obs;
     const float *mission;
-    const unsigned char *cameras; /* may be NULL */
+    const void *cameras; /* u8 or f32 camera rows; may be NULL */
     float *features;
     unsigned long long batch;
     unsigned long long wait_ns;
     long long stall_sample; /* test hook: >= 0 withholds that sample's copies */
 };
 
-__global__ void __launch_bounds__(kThreads, 2) features_staged_kernel(const StagedArgs a) {
+template <bool kF32Cam>
+__global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
+    features_staged_kernel(const StagedArgs a) {
+    using R = Ring<kF32Cam>;
     extern __shared__ __align__(128) unsigned char smem[];
-    const uint32_t full_bar = smem_addr(smem);            /* kStages x 8 B */
-    const uint32_t empty_bar = full_bar + 8 * kStages;     /* kStages x 8 B */
+    const uint32_t full_bar = smem_addr(smem);            /* R::stages x 8 B */
+    const uint32_t empty_bar = full_bar + 8 * R::stages;   /* R::stages x 8 B */
     unsigned char *stages = smem + kBarrierRegion;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < R::stages; ++s) {
             mbar_init(full_bar + 8 * s, 1);
             mbar_init(empty_bar + 8 * s, kConsumerWarps);
         }
@@ -266,30 +301,30 @@ __global__ void __launch_bounds__(kThreads, 2) features_staged_kernel(const Stag
     if (warp == kConsumerWarps) {
         /* ---------------- producer warp ---------------- */
         const uint64_t policy = evict_first_policy();
-        const uint32_t tx_bytes = kObsBytes + (a.cameras ? kCameraBytes : 0u);
+        const uint32_t tx_bytes = kObsBytes + (a.cameras ? R::camera_bytes : 0u);
+        const unsigned char *cameras = static_cast<const unsigned char *>(a.cameras);
         unsigned long long k = 0;
         bool ok = true;
         for (unsigned long long sample = first; sample < a.batch; sample += step, ++k) {
-            const int s = static_cast<int>(k % kStages);
-            const uint32_t phase = static_cast<uint32_t>((k / kStages) & 1);
+            const int s = static_cast<int>(k % R::stages);
+            const uint32_t phase = static_cast<uint32_t>((k / R::stages) & 1);
             /* warp-uniform: every lane leaves together or none does */
             if (!__all_sync(0xffffffffu, mbar_wait(empty_bar + 8 * s, phase ^ 1u, a.wait_ns))) {
                 ok = false;
                 break;
             }
             if (static_cast<long long>(sample) == a.stall_sample) continue; /* test hook */
-            const uint32_t stage = smem_addr(stages + static_cast<size_t>(s) * kStageBytes);
+            const uint32_t stage = smem_addr(stages + static_cast<size_t>(s) * R::stage_bytes);
             if (lane < kMissionDim) {
-                async_load4(stage + kStageMissionOff + 4 * lane,
-                            a.mission + sample * kMissionDim + lane);
+                async_load4(stage + R::mission_off + 4 * lane, a.mission + sample * kMissionDim + lane);
                 async_track(full_bar + 8 * s);
             }
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive_expect_tx(full_bar + 8 * s, tx_bytes);
                 bulk_load(stage, a.obs + sample * kObsDim, kObsBytes, full_bar + 8 * s, policy);
-                if (a.cameras)
-                    bulk_load(stage + kStageCamOff, a.cameras + sample * kCameraBytes, kCameraBytes,
+                if (cameras)
+                    bulk_load(stage + R::cam_off, cameras + sample * R::camera_bytes, R::camera_bytes,
                               full_bar + 8 * s, policy);
             }
             __syncwarp();
@@ -298,9 +333,9 @@ __global__ void __launch_bounds__(kThreads, 2) features_staged_kernel(const Stag
             if (lane == 0) atomicOr(&g_feature_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
             /* Drain this CTA's outstanding copies before exiting (bounded). */
             const unsigned long long issued = k;
-            const unsigned long long lo = issued > kStages ? issued - kStages : 0;
+            const unsigned long long lo = issued > R::stages ? issued - R::stages : 0;
             for (unsigned long long j = lo; j < issued; ++j)
-                mbar_wait(full_bar + 8 * (j % kStages), static_cast<uint32_t>((j / kStages) & 1),
+                mbar_wait(full_bar + 8 * (j % R::stages), static_cast<uint32_t>((j / R::stages) & 1),
                           a.wait_ns);
         }
         return;
@@ -313,37 +348,67 @@ __global__ void __launch_bounds__(kThreads, 2) features_staged_kernel(const Stag
     const int qy = warp & 1;
     unsigned long long k = 0;
     for (unsigned long long sample = first; sample < a.batch; sample += step, ++k) {
-        const int s = static_cast<int>(k % kStages);
-        const uint32_t phase = static_cast<uint32_t>((k / kStages) & 1);
+        const int s = static_cast<int>(k % R::stages);
+        const uint32_t phase = static_cast<uint32_t>((k / R::stages) & 1);
         if (!__all_sync(0xffffffffu, mbar_wait(full_bar + 8 * s, phase, a.wait_ns))) {
             if (lane == 0) atomicOr(&g_feature_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
             return;
         }
-        const unsigned char *stage = stages + static_cast<size_t>(s) * kStageBytes;
+        const unsigned char *stage = stages + static_cast<size_t>(s) * R::stage_bytes;
         const float *o = reinterpret_cast<const float *>(stage);
-        const float *m = reinterpret_cast<const float *>(stage + kStageMissionOff);
+        const float *m = reinterpret_cast<const float *>(stage + R::mission_off);
 
         /* LiDAR: lane covers bins 4*lane..4*lane+3 of the warp's four rows;
          * all 16 values belong to sector (head, el_sector, lane/4). */
         const float4 *rows = reinterpret_cast<const float4 *>(o + kLidarOffset) +
                              (head * 16 + el_sector * 4) * 32 + lane;
         const float4 r0 = rows[0], r1 = rows[32], r2 = rows[64], r3 = rows[96];
-
-        /* Camera half-image: lane reads 16-byte chunks lane, lane+32, ...;
-         * chunk c sits in row c/4, columns 16*(c%4).., so quadrant x = bit 1. */
-        uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0, c2 = c0, c3 = c0;
-        if (a.cameras) {
-            const uint4 *half = reinterpret_cast<const uint4 *>(stage + kStageCamOff) +
-                                cam * 256 + qy * 128 + lane;
-            c0 = half[0]; c1 = half[32]; c2 = half[64]; c3 = half[96];
-        }
         float scalar = 0.0f;
         const int t = warp * 32 + lane;
         if (t < 62) scalar = scalar_feature(t, o, m);
 
-        /* All shared-memory reads of this stage are done: release it. */
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar + 8 * s);
+        /* Camera half-image (camera w/2, rows 32*(w&1)..+31). */
+        uint32_t bytes = 0;      /* u8: integer byte sum */
+        float luma = 0.0f;       /* f32: sum of quantised bytes, exact in float */
+        if constexpr (!kF32Cam) {
+            /* 16-byte chunk c (c = lane, lane+32, ...) sits in row c/4,
+             * columns 16*(c%4).., so quadrant x = lane bit 1. */
+            uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0, c2 = c0, c3 = c0;
+            if (a.cameras) {
+                const uint4 *half = reinterpret_cast<const uint4 *>(stage + R::cam_off) +
+                                    cam * 256 + qy * 128 + lane;
+                c0 = half[0]; c1 = half[32]; c2 = half[64]; c3 = half[96];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar + 8 * s); /* stage fully read: release it */
+            bytes = byte_sum4(c0.x, bytes); bytes = byte_sum4(c0.y, bytes);
+            bytes = byte_sum4(c0.z, bytes); bytes = byte_sum4(c0.w, bytes);
+            bytes = byte_sum4(c1.x, bytes); bytes = byte_sum4(c1.y, bytes);
+            bytes = byte_sum4(c1.z, bytes); bytes = byte_sum4(c1.w, bytes);
+            bytes = byte_sum4(c2.x, bytes); bytes = byte_sum4(c2.y, bytes);
+            bytes = byte_sum4(c2.z, bytes); bytes = byte_sum4(c2.w, bytes);
+            bytes = byte_sum4(c3.x, bytes); bytes = byte_sum4(c3.y, bytes);
+            bytes = byte_sum4(c3.z, bytes); bytes = byte_sum4(c3.w, bytes);
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, 1);
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, 4);
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, 8);
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, 16);
+        } else {
+            /* float4 chunk c (c = lane, lane+32, ...) sits in row c/16,
+             * columns 4*(c%16).., so quadrant x = lane bit 3. */
+            if (a.cameras) {
+                const float4 *half = reinterpret_cast<const float4 *>(stage + R::cam_off) +
+                                     cam * 1024 + qy * 512 + lane;
+#pragma unroll 4
+                for (int i = 0; i < 16; ++i) luma += luma_bytes4(half[32 * i]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar + 8 * s); /* stage fully read: release it */
+            luma += __shfl_xor_sync(0xffffffffu, luma, 1);
+            luma += __shfl_xor_sync(0xffffffffu, luma, 2);
+            luma += __shfl_xor_sync(0xffffffffu, luma, 4);
+            luma += __shfl_xor_sync(0xffffffffu, luma, 16);
+        }
 
         float sum = 0.0f;
         int counts = 0;
@@ -356,25 +421,15 @@ __global__ void __launch_bounds__(kThreads, 2) features_staged_kernel(const Stag
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
         counts += __shfl_xor_sync(0xffffffffu, counts, 2);
 
-        uint32_t bytes = 0;
-        bytes = byte_sum4(c0.x, bytes); bytes = byte_sum4(c0.y, bytes);
-        bytes = byte_sum4(c0.z, bytes); bytes = byte_sum4(c0.w, bytes);
-        bytes = byte_sum4(c1.x, bytes); bytes = byte_sum4(c1.y, bytes);
-        bytes = byte_sum4(c1.z, bytes); bytes = byte_sum4(c1.w, bytes);
-        bytes = byte_sum4(c2.x, bytes); bytes = byte_sum4(c2.y, bytes);
-        bytes = byte_sum4(c2.z, bytes); bytes = byte_sum4(c2.w, bytes);
-        bytes = byte_sum4(c3.x, bytes); bytes = byte_sum4(c3.y, bytes);
-        bytes = byte_sum4(c3.z, bytes); bytes = byte_sum4(c3.w, bytes);
-        bytes += __shfl_xor_sync(0xffffffffu, bytes, 1);
-        bytes += __shfl_xor_sync(0xffffffffu, bytes, 4);
-        bytes += __shfl_xor_sync(0xffffffffu, bytes, 8);
-        bytes += __shfl_xor_sync(0xffffffffu, bytes, 16);
-
         float *f = a.features + sample * kFeatureDim;
         if ((lane & 3) == 0)
             f[62 + head * 32 + el_sector * 8 + (lane >> 2)] = lidar_sector_mean(sum, counts);
-        if (lane == 0 || lane == 2)
-            f[126 + cam * 4 + qy * 2 + (lane >> 1)] = camera_feature(bytes);
+        if constexpr (!kF32Cam) {
+            if (lane == 0 || lane == 2) f[126 + cam * 4 + qy * 2 + (lane >> 1)] = camera_feature(bytes);
+        } else {
+            if (lane == 0 || lane == 8)
+                f[126 + cam * 4 + qy * 2 + (lane >> 3)] = __fdiv_rn(luma, 1024.0f * 255.0f);
+        }
         if (t < 62) f[t] = scalar;
     }
 }
@@ -383,9 +438,9 @@ __global__ void __launch_bounds__(kThreads, 2) features_staged_kernel(const Stag
 /* Direct kernel for rows that are not 16-byte aligned: one warp per
  * aircraft, plain loads, same arithmetic. */
 
+template <bool kF32Cam>
 __global__ void __launch_bounds__(256) features_direct_kernel(const float *obs, const float *mission,
-                                                              const unsigned char *cameras,
-                                                              float *features,
+                                                              const void *cameras, float *features,
                                                               unsigned long long batch) {
     const int lane = threadIdx.x & 31;
     const unsigned long long warps = (static_cast<unsigned long long>(gridDim.x) * blockDim.x) >> 5;
@@ -411,17 +466,34 @@ __global__ void __launch_bounds__(256) features_direct_kernel(const float *obs, 
             counts += __shfl_xor_sync(0xffffffffu, counts, 2);
             if ((lane & 3) == 0) f[62 + band * 8 + (lane >> 2)] = lidar_sector_mean(sum, counts);
         }
-        for (int half = 0; half < 8; ++half) { /* camera * 2 + qy */
-            unsigned int bytes = 0;
-            if (cameras) {
-                const unsigned char *px = cameras + sample * kCameraBytes + half * 2048 + 2 * lane;
-                for (int y = 0; y < 32; ++y) bytes += px[y * 64] + px[y * 64 + 1];
+        for (int half = 0; half < 8; ++half) { /* camera * 2 + qy; lane covers columns 2*lane, +1 */
+            float value = 0.0f;
+            if constexpr (!kF32Cam) {
+                unsigned int bytes = 0;
+                if (cameras) {
+                    const unsigned char *px = static_cast<const unsigned char *>(cameras) +
+                                              sample * kCameraBytes + half * 2048 + 2 * lane;
+                    for (int y = 0; y < 32; ++y) bytes += px[y * 64] + px[y * 64 + 1];
+                }
+                bytes += __shfl_xor_sync(0xffffffffu, bytes, 1);
+                bytes += __shfl_xor_sync(0xffffffffu, bytes, 2);
+                bytes += __shfl_xor_sync(0xffffffffu, bytes, 4);
+                bytes += __shfl_xor_sync(0xffffffffu, bytes, 8);
+                value = camera_feature(bytes);
+            } else {
+                float luma = 0.0f;
+                if (cameras) {
+                    const float *px = static_cast<const float *>(cameras) + sample * kCameraBytes +
+                                      half * 2048 + 2 * lane;
+                    for (int y = 0; y < 32; ++y) luma += luma_byte(px[y * 64]) + luma_byte(px[y * 64 + 1]);
+                }
+                luma += __shfl_xor_sync(0xffffffffu, luma, 1);
+                luma += __shfl_xor_sync(0xffffffffu, luma, 2);
+                luma += __shfl_xor_sync(0xffffffffu, luma, 4);
+                luma += __shfl_xor_sync(0xffffffffu, luma, 8);
+                value = __fdiv_rn(luma, 1024.0f * 255.0f);
             }
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, 1);
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, 2);
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, 4);
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, 8);
-            if (lane == 0 || lane == 16) f[126 + half * 2 + (lane >> 4)] = camera_feature(bytes);
+            if (lane == 0 || lane == 16) f[126 + half * 2 + (lane >> 4)] = value;
         }
         f[lane] = scalar_feature(lane, o, m);
         if (lane + 32 < 62) f[lane + 32] = scalar_feature(lane + 32, o, m);
@@ -435,25 +507,34 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
     std::atomic<int> ready{0};
     int sms = 0;
-    int staged_blocks_per_sm = 0;
+    int blocks_per_sm[2] = {0, 0}; /* staged kernel, u8 / f32 cameras */
 };
 DeviceInfo g_devices[kMaxDevices];
+
+template <bool kF32Cam>
+cudaError_t staged_occupancy(int *blocks) {
+    cudaError_t st = cudaFuncSetAttribute(features_staged_kernel<kF32Cam>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(Ring<kF32Cam>::smem_bytes));
+    if (st != cudaSuccess) return st;
+    st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, features_staged_kernel<kF32Cam>, kThreads,
+                                                       Ring<kF32Cam>::smem_bytes);
+    if (*blocks < 1) *blocks = 1;
+    return st;
+}
 
 cudaError_t device_info(int dev, const DeviceInfo **out) {
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     DeviceInfo &d = g_devices[dev];
     if (!d.ready.load(std::memory_order_acquire)) {
-        int sms = 0, blocks = 0;
+        int sms = 0, b8 = 0, b32 = 0;
         cudaError_t st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (st != cudaSuccess) return st;
-        st = cudaFuncSetAttribute(features_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(kSmemBytes));
-        if (st != cudaSuccess) return st;
-        st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, features_staged_kernel, kThreads,
-                                                           kSmemBytes);
+        if (st == cudaSuccess) st = staged_occupancy<false>(&b8);
+        if (st == cudaSuccess) st = staged_occupancy<true>(&b32);
         if (st != cudaSuccess) return st;
         d.sms = sms;
-        d.staged_blocks_per_sm = blocks > 0 ? blocks : 1;
+        d.blocks_per_sm[0] = b8;
+        d.blocks_per_sm[1] = b32;
         d.ready.store(1, std::memory_order_release);
     }
     *out = &d;
@@ -469,13 +550,14 @@ bool aligned(const void *p, uintptr_t n) {
 /* ------------------------------------------------------------------ */
 /* Internal launch used by the public shim and by the tests' hooks. */
 
-extern "C" int tb_features_launch_checked(const float *obs, const float *mission,
-                                          const unsigned char *cameras, float *features,
-                                          size_t batch, void *stream,
-                                          const tb_features_launch_opts *opts, int *launch_error) {
+template <bool kF32Cam>
+static int launch_features(const float *obs, const float *mission, const void *cameras, float *features,
+                           size_t batch, void *stream, const tb_features_launch_opts *opts,
+                           int *launch_error) {
     if (launch_error) *launch_error = static_cast<int>(cudaErrorInvalidValue);
     if (!obs || !mission || !features || batch == 0 || batch > 0x7fffffffu) return 0;
     if (!aligned(obs, 4) || !aligned(mission, 4) || !aligned(features, 4)) return 0;
+    if (kF32Cam && cameras && !aligned(cameras, 4)) return 0;
     int dev = 0;
     cudaError_t st = cudaGetDevice(&dev);
     const DeviceInfo *info = nullptr;
@@ -501,22 +583,35 @@ extern "C" int tb_features_launch_checked(const float *obs, const float *mission
         args.wait_ns = (opts && opts->wait_ns) ? opts->wait_ns : kDefaultWaitNs;
         args.stall_sample = opts ? opts->stall_sample : -1;
         unsigned long long grid = static_cast<unsigned long long>(info->sms) *
-                                  static_cast<unsigned long long>(info->staged_blocks_per_sm);
+                                  static_cast<unsigned long long>(info->blocks_per_sm[kF32Cam ? 1 : 0]);
         if (opts && opts->grid_limit > 0 && grid > static_cast<unsigned long long>(opts->grid_limit))
             grid = static_cast<unsigned long long>(opts->grid_limit);
         if (grid > batch) grid = batch;
-        features_staged_kernel<<<static_cast<unsigned int>(grid), kThreads, kSmemBytes, s>>>(args);
+        features_staged_kernel<kF32Cam>
+            <<<static_cast<unsigned int>(grid), kThreads, Ring<kF32Cam>::smem_bytes, s>>>(args);
     } else {
-        const unsigned long long warps_needed = batch;
-        unsigned long long grid = (warps_needed + 7) / 8;
+        unsigned long long grid = (batch + 7) / 8; /* 8 warps of 32, one aircraft per warp */
         const unsigned long long cap = static_cast<unsigned long long>(info->sms) * 8;
         if (grid > cap) grid = cap;
-        features_direct_kernel<<<static_cast<unsigned int>(grid), 256, 0, s>>>(obs, mission, cameras,
-                                                                                features, batch);
+        features_direct_kernel<kF32Cam>
+            <<<static_cast<unsigned int>(grid), 256, 0, s>>>(obs, mission, cameras, features, batch);
     }
     st = cudaGetLastError();
     if (launch_error) *launch_error = static_cast<int>(st);
     return st == cudaSuccess;
+}
+
+extern "C" int tb_features_launch_checked(const float *obs, const float *mission,
+                                          const unsigned char *cameras, float *features,
+                                          size_t batch, void *stream,
+                                          const tb_features_launch_opts *opts, int *launch_error) {
+    return launch_features<false>(obs, mission, cameras, features, batch, stream, opts, launch_error);
+}
+
+extern "C" int tb_features_launch_f32cam(const float *obs, const float *mission,
+                                         const float *cameras_f32, float *features, size_t batch,
+                                         void *stream, const tb_features_launch_opts *opts) {
+    return launch_features<true>(obs, mission, cameras_f32, features, batch, stream, opts, nullptr);
 }
 
 extern "C" int tb_features_launch(const float *obs, const float *mission,
@@ -549,11 +644,11 @@ extern "C" int tb_features_staged_config(int *blocks_per_sm, int *sms, int *smem
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;
     const DeviceInfo *info = nullptr;
     if (device_info(dev, &info) != cudaSuccess) return 0;
-    if (blocks_per_sm) *blocks_per_sm = info->staged_blocks_per_sm;
+    if (blocks_per_sm) *blocks_per_sm = info->blocks_per_sm[0];
     if (sms) *sms = info->sms;
-    if (smem_bytes) *smem_bytes = static_cast<int>(kSmemBytes);
+    if (smem_bytes) *smem_bytes = static_cast<int>(Ring<false>::smem_bytes);
     if (threads) *threads = kThreads;
-    if (stages) *stages = kStages;
+    if (stages) *stages = Ring<false>::stages;
     return 1;
 }
 
@@ -572,4 +667,15 @@ extern "C" int tb_cuda_synchronize(void *stream) {
     unsigned int features = 0, onboard = 0;
     if (!tb_features_status_take(stream, &features) || !tb_onboard_status_take(stream, &onboard)) return 0;
     return (features | onboard) == 0;
+}
+
+/* ---- additive entry point: FP32 cameras ---- */
+
+extern "C" int tb_cuda_extract_features_device_f32cam(const float *device_obs,
+                                                      const float *device_mission,
+                                                      const float *device_cameras_f32,
+                                                      float *device_features, size_t batch_size,
+                                                      void *stream) {
+    return tb_features_launch_f32cam(device_obs, device_mission, device_cameras_f32, device_features,
+                                     batch_size, stream, nullptr);
 }

@@ -43,6 +43,12 @@ int tb_features_launch_checked(const float *obs, const float *mission,
                                void *stream, const tb_features_launch_opts *opts,
                                int *launch_error);
 
+/* As tb_features_launch, with FP32 camera rows [batch,16384] quantised on
+ * load with the simulator's rule. */
+int tb_features_launch_f32cam(const float *obs, const float *mission, const float *cameras_f32,
+                              float *features, size_t batch, void *stream,
+                              const tb_features_launch_opts *opts);
+
 /* Reads (via `stream`) and clears the current device's kernel status word.
  * Returns 1 if the read succeeded; *status receives the bits. */
 int tb_features_status_take(void *stream, unsigned int *status);

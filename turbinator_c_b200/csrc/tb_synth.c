@@ -29,8 +29,8 @@ static float synth_signed(uint64_t *state) {
 }
 
 uint8_t tb_synth_quantize(float v) {
-    v = v < 0.0f ? 0.0f : (v > 1.0f ? 1.0f : v);
-    return (uint8_t)roundf(v * 255.0f);
+    /* The simulator's rule in double: fmax(0, fmin(255, round(v * 255))). */
+    return (uint8_t)fmax(0.0, fmin(255.0, round((double)v * 255.0)));
 }
 
 static void synth_sample(uint64_t seed, uint64_t index, int mode, float *o, float *m,

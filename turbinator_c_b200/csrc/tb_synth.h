@@ -39,8 +39,9 @@ int tb_synth_generate(uint64_t seed, uint64_t first, size_t count, int mode,
                       float *obs, float *mission, uint8_t *cameras_u8, float *cameras_f32,
                       int threads);
 
-/* The simulator's luma quantisation for one [0,1] camera value
- * (sensors.c:67): round-half-away of clamp(v,0,1)*255 in float. */
+/* The simulator's luma quantisation of one camera value (src/sim/sensors.c:67
+ * with the clamp of src/sim/sim_internal.h:73), in double:
+ * fmax(0, fmin(255, round(v * 255))); NaN gives 255. */
 uint8_t tb_synth_quantize(float v);
 
 #ifdef __cplusplus
