@@ -66,7 +66,11 @@ const char *tb_cuda_feature_batch_error(const tb_cuda_feature_batch *batch);
  * cameras are required.  0 < count <= max_batch.  Copies in, extracts and
  * copies out, returning after the features are in out_features_142.
  * Page-locked host buffers are streamed in chunks so that copies and
- * kernels overlap; pageable buffers work too, at pageable copy speed.
+ * kernels overlap.  Pageable buffers of 512 or more rows per device are
+ * copied by up to 8 host threads per device (TB_CUDA_HOST_THREADS overrides
+ * the total, read when the handle is created) through the handle's
+ * page-locked staging, overlapping host copies, transfers and kernels;
+ * smaller pageable calls are copied by the driver on the calling thread.
  * Returns 1, or 0 with a stage-named message in
  * tb_cuda_feature_batch_error().  A handle is not thread-safe. */
 int tb_cuda_extract_features_host(tb_cuda_feature_batch *batch,
@@ -77,6 +81,19 @@ int tb_cuda_extract_features_host(tb_cuda_feature_batch *batch,
                                   float *out_features_142);
 
 /* ---- Additive entry points ---- */
+
+/* A handle whose calls are sharded by sample over several GPUs (no
+ * counterpart in the reference, which drives one device per handle).
+ * device_ids[0..device_count) (1 <= device_count <= 16; an id may repeat);
+ * each device holds staging for ceil(max_batch / device_count) samples.
+ * tb_cuda_extract_features_host on it splits the rows into contiguous
+ * per-device slices, extracts them concurrently (one or more host threads
+ * per device) and gathers the features into out_features_142 in row order.
+ * tb_cuda_feature_batch_destroy and _error apply unchanged.  Makes
+ * device_ids[0] current on the calling thread.  NULL on failure. */
+tb_cuda_feature_batch *tb_cuda_feature_batch_create_multi(const int *device_ids,
+                                                          int device_count,
+                                                          size_t max_batch);
 
 /* Onboard tactical (24) and physics-prior (15) values per aircraft: the
  * reference's device-only src/network/onboard_features.cuh:515-519

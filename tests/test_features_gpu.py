@@ -179,3 +179,71 @@ def test_bounded_pipeline_wait_reports_and_recovers():
     assert tb.tb_cuda_synchronize() == 0
     assert tb.tb_cuda_synchronize() == 1          # reported once, then cleared
     check_features(run_device(obs, mission, cams), oracle.features(obs, mission, cams), "after-timeout")
+
+
+@pytest.mark.parametrize("pin_in,pin_out", [(False, False), (True, False), (False, True)])
+def test_host_abi_buffer_kinds_threaded(pin_in, pin_out):
+    """Pageable inputs go through the handle's page-locked staging on several
+    host threads; page-locked ones are streamed directly; either output kind."""
+    n = 9000
+    obs, mission, cams, _ = tb.generate(28, 0, n, pinned=pin_in)
+    out = (torch.zeros((n, 142), dtype=torch.float32, pin_memory=True).numpy() if pin_out
+           else np.zeros((n, 142), np.float32))
+    with tb.FeatureBatch(0, n) as fb:
+        assert fb.extract(obs, mission, cams, n, out) == 1, fb.error()
+        expected = oracle.features(np.asarray(obs), np.asarray(mission), np.asarray(cams))
+        check_features(out, expected, f"host pin_in={pin_in} pin_out={pin_out}")
+        # a second, smaller call reuses the same staging
+        part = np.zeros((777, 142), np.float32)
+        assert fb.extract(obs[1000:1777], mission[1000:1777], cams[1000:1777], 777, part) == 1
+        check_features(part, expected[1000:1777], "host second call")
+
+
+def test_trainer_style_small_calls():
+    """The trainer's pattern: a small persistent batch extracted again and
+    again from pageable buffers (src/trainer/main.c:526-673)."""
+    obs, mission, cams, _ = tb.generate(29, 0, 32)
+    expected = oracle.features(obs, mission, cams)
+    out = np.zeros((32, 142), np.float32)
+    with tb.FeatureBatch(0, 32) as fb:
+        for count in (32, 8, 1, 32):
+            out[:] = 0
+            assert fb.extract(obs, mission, cams, count, out) == 1, fb.error()
+            check_features(out[:count], expected[:count], f"trainer count={count}")
+
+
+@pytest.mark.parametrize("devices,n", [([0, 0], 5001), ([0, 0, 0], 3), ([0, 0, 0], 12000)])
+def test_multi_device_handle_shards_and_gathers(devices, n):
+    """A sample-sharded handle (the same GPU listed several times here; the
+    slicing and gather are the same as over distinct GPUs)."""
+    obs, mission, cams, _ = tb.generate(30, 0, n)
+    out = np.zeros((n, 142), np.float32)
+    with tb.FeatureBatch(devices, n) as fb:
+        assert fb.extract(obs, mission, cams, n, out) == 1, fb.error()
+    check_features(out, oracle.features(obs, mission, cams), f"multi {devices}")
+
+
+def test_multi_device_handle_rejects_bad_devices():
+    assert tb.tb_cuda_feature_batch_create_multi([0, 10_000], 16) is None
+    assert tb.tb_cuda_feature_batch_create_multi([], 16) is None
+    obs, mission, cams, _ = tb.generate(31, 0, 4)
+    check_features(run_device(obs, mission, cams), oracle.features(obs, mission, cams), "after bad multi create")
+
+
+def test_host_abi_reports_pipeline_timeout_once():
+    """The kernels' status word is per device and sticky until read: a
+    pipeline whose bounded waits expired makes the next host call fail with
+    the stage-named message, and the call after it succeeds."""
+    obs, mission, cams, _ = tb.generate(32, 0, 16)
+    d_obs, d_mis, d_cam = _dev(obs), _dev(mission), _dev(cams)
+    d_out = torch.zeros((16, 142), device="cuda")
+    assert tb.take_status() == 0
+    assert tb.launch(d_obs, d_mis, d_cam, d_out, 16, None, wait_ns=20_000_000, stall_sample=3) == 1
+    torch.cuda.synchronize()
+    out = np.zeros((16, 142), np.float32)
+    with tb.FeatureBatch(0, 16) as fb:
+        assert fb.extract(obs, mission, cams, 16, out) == 0
+        assert "feature pipeline wait timed out" in fb.error()
+        assert fb.extract(obs, mission, cams, 16, out) == 1, fb.error()
+        assert fb.error() == ""
+    check_features(out, oracle.features(obs, mission, cams), "after reported timeout")

@@ -74,6 +74,7 @@ def load_library() -> ctypes.CDLL:
     _bind(lib, "tb_cuda_extract_features_device", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
     _bind(lib, "tb_cuda_synchronize", _c.c_int, [_vp])
     _bind(lib, "tb_cuda_feature_batch_create", _vp, [_c.c_int, _sz])
+    _bind(lib, "tb_cuda_feature_batch_create_multi", _vp, [_c.POINTER(_c.c_int), _c.c_int, _sz])
     _bind(lib, "tb_cuda_feature_batch_destroy", None, [_vp])
     _bind(lib, "tb_cuda_feature_batch_error", _c.c_char_p, [_vp])
     _bind(lib, "tb_cuda_extract_features_host", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
@@ -208,11 +209,20 @@ def staged_config() -> dict:
     return {k: v.value for k, v in zip(keys, vals)}
 
 
-class FeatureBatch:
-    """RAII wrapper over a ``tb_cuda_feature_batch`` handle (host-pointer ABI)."""
+def tb_cuda_feature_batch_create_multi(device_ids, max_batch: int) -> Optional[int]:
+    ids = (_c.c_int * len(device_ids))(*device_ids)
+    return load_library().tb_cuda_feature_batch_create_multi(ids, len(device_ids), max_batch)
 
-    def __init__(self, device_id: int, max_batch: int):
-        self.handle = tb_cuda_feature_batch_create(device_id, max_batch)
+
+class FeatureBatch:
+    """RAII wrapper over a ``tb_cuda_feature_batch`` handle (host-pointer ABI).
+    ``device_id`` may be a list of devices for a sample-sharded handle."""
+
+    def __init__(self, device_id, max_batch: int):
+        if isinstance(device_id, (list, tuple)):
+            self.handle = tb_cuda_feature_batch_create_multi(list(device_id), max_batch)
+        else:
+            self.handle = tb_cuda_feature_batch_create(device_id, max_batch)
         if not self.handle:
             raise RuntimeError(f"tb_cuda_feature_batch_create({device_id}, {max_batch}) failed")
         self.max_batch = max_batch

@@ -638,6 +638,19 @@ extern "C" int tb_features_status_take(void *stream, unsigned int *status) {
     return 1;
 }
 
+extern "C" int tb_features_status_enqueue(void *stream, unsigned int *host_word) {
+    return cudaMemcpyFromSymbolAsync(host_word, g_feature_status, sizeof(unsigned int), 0,
+                                     cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)) == cudaSuccess;
+}
+
+extern "C" int tb_features_status_clear(void *stream) {
+    static const unsigned int zero = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return cudaMemcpyToSymbolAsync(g_feature_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) ==
+               cudaSuccess &&
+           cudaStreamSynchronize(s) == cudaSuccess;
+}
+
 extern "C" int tb_features_staged_config(int *blocks_per_sm, int *sms, int *smem_bytes,
                                          int *threads, int *stages) {
     int dev = 0;

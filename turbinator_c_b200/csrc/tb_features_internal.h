@@ -53,6 +53,13 @@ int tb_features_launch_f32cam(const float *obs, const float *mission, const floa
  * Returns 1 if the read succeeded; *status receives the bits. */
 int tb_features_status_take(void *stream, unsigned int *status);
 
+/* Enqueue on `stream` an asynchronous copy of the current device's status
+ * word into host_word (page-locked), to be read after the stream drains. */
+int tb_features_status_enqueue(void *stream, unsigned int *host_word);
+
+/* Clear the current device's status word (synchronous on `stream`). */
+int tb_features_status_clear(void *stream);
+
 /* As tb_features_status_take, for the onboard kernel's own status word. */
 int tb_onboard_status_take(void *stream, unsigned int *status);
 
