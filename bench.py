@@ -60,6 +60,7 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=4.0, help="target wall time of the CPU sample")
     p.add_argument("--no-onboard", action="store_true", help="skip the onboard tactical/prior leg")
     p.add_argument("--no-f32cam", action="store_true", help="skip the FP32-camera entry-point leg")
+    p.add_argument("--no-actor-inputs", action="store_true", help="skip the learner-input leg")
     return p.parse_args()
 
 
@@ -383,6 +384,37 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         del d_camf
         torch.cuda.empty_cache()
 
+    # ---- learner input tensors (tb_cuda_prepare_actor_inputs_device) on the same rows
+    actor = None
+    if not args.no_actor_inputs:
+        shapes = ((count, 91), (count, 49), (count, 24), (count, 15), (count, 6 * 2048), (count, 16384))
+        a_outs = [torch.empty(sh, dtype=torch.float32, device=dev) for sh in shapes]
+        for _ in range(max(args.warmup, 3)):
+            assert tb.tb_cuda_prepare_actor_inputs_device(d_obs, d_mis, d_cam, *a_outs, count, stream) == 1
+        torch.cuda.synchronize(dev)
+        barrier()
+        a_start, a_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_steps = max(1, min(args.steps, 20))
+        a_start.record(stream)
+        for _ in range(a_steps):
+            tb.tb_cuda_prepare_actor_inputs_device(d_obs, d_mis, d_cam, *a_outs, count, stream)
+        a_end.record(stream)
+        torch.cuda.synchronize(dev)
+        a_per = a_start.elapsed_time(a_end) / 1e3 / a_steps
+        a_per_max = max_over_ranks(a_per)
+        bpa = tb.BYTES_PER_SAMPLE_ACTOR_INPUTS
+        peak_gbs, peak_kind = measured_hbm_peak()
+        a_ach = count * bpa / a_per / 1e9
+        actor = {"entry_point": "tb_cuda_prepare_actor_inputs_device",
+                 "outputs": "proprio 91, mission 49, tactical 24, prior 15, LiDAR 6x2048, luma 16384 per aircraft",
+                 "value": total / a_per_max, "unit": UNIT, "ms_per_launch": a_per_max * 1e3,
+                 "bytes_per_sample": bpa,
+                 "roofline": {"bound": "hbm (78 % writes)", "achieved": a_ach, "peak": peak_gbs, "unit": "GB/s",
+                              "frac": a_ach / peak_gbs, "peak_source": f"{peak_kind} hbm_gbs (copy)"},
+                 "launches": 2 * a_steps}
+        del a_outs
+        torch.cuda.empty_cache()
+
     # ---- secondary path: onboard tactical/prior values on the same resident inputs
     onboard = None
     if not args.no_onboard:
@@ -477,14 +509,17 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                      "algorithmic_bytes_per_launch": count * tb.BYTES_PER_SAMPLE,
                      "kernel": "features_staged_kernel", "avg_launch_ms": avg_launch_s * 1e3},
         "gpu_launches": (args.steps + e2e_steps * chunks + (onboard["launches"] if onboard else 0) +
-                         (f32cam["launches"] if f32cam else 0)),
+                         (f32cam["launches"] if f32cam else 0) + (actor["launches"] if actor else 0)),
         "gpu_launches_detail": {"value_region": args.steps, "e2e_region": e2e_steps * chunks,
                                 "onboard_regions": onboard["launches"] if onboard else 0,
-                                "f32cam_region": f32cam["launches"] if f32cam else 0},
+                                "f32cam_region": f32cam["launches"] if f32cam else 0,
+                                "actor_inputs_region": actor["launches"] if actor else 0},
         "clocks": clk,
     }
     if f32cam is not None:
         line["f32_cameras"] = f32cam
+    if actor is not None:
+        line["actor_inputs"] = actor
     if onboard is not None:
         line["onboard"] = onboard
     if world == 1 and not args.no_cpu_baseline:

@@ -128,6 +128,32 @@ int tb_cuda_extract_features_device_f32cam(const float *device_obs,
                                            size_t batch_size,
                                            void *stream);
 
+/* Input tensors of the reference's 618M learner, built from the same rows in
+ * one call (no C entry point in the reference: its actor forward pass builds
+ * them with scalar_inputs, lidar_channels and camera_luma,
+ * src/network/network_gpu.cu:274-303,467-483,1446-1451).  Device pointers,
+ * one row per aircraft:
+ *   proprio [batch,91]    52 symlog-scaled proprioception values, then the
+ *                         24 tactical and 15 prior values
+ *   mission [batch,49]    mission (non-finite -> 0), tactical, prior
+ *   tactical [batch,24], prior [batch,15]  as tb_cuda_extract_onboard_device
+ *   lidar [batch,6,2048]  per head: inverse range, range/30, return flag
+ *   luma [batch,16384]    camera byte / 255 - 0.5
+ * obs, cameras, lidar and luma must be 16-byte aligned, the rest 4-byte
+ * aligned; cameras are required.  Returns 1 if the launches succeeded, 0
+ * otherwise; asynchronous on `stream`. */
+int tb_cuda_prepare_actor_inputs_device(const float *device_obs,
+                                        const float *device_mission,
+                                        const unsigned char *device_cameras,
+                                        float *device_proprio_91,
+                                        float *device_mission_49,
+                                        float *device_tactical_24,
+                                        float *device_prior_15,
+                                        float *device_lidar_6x2048,
+                                        float *device_camera_luma,
+                                        size_t batch_size,
+                                        void *stream);
+
 /* Largest count accepted by tb_cuda_extract_features_host_noalloc. */
 #define TB_CUDA_NOALLOC_MAX_BATCH 64
 

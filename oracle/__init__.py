@@ -20,6 +20,7 @@ ORACLE_PATH = os.path.join(HERE, "liboracle.so")
 REF_TRAINING_PATH = os.path.join(HERE, "_ref", "libtb_ref_training.so")
 REF_ONBOARD_PATH = os.path.join(HERE, "_ref", "libtb_ref_onboard.so")
 REF_ONBOARD_CR_PATH = os.path.join(HERE, "_ref", "libtb_ref_onboard_cr.so")
+REF_ACTOR_INPUTS_PATH = os.path.join(HERE, "_ref", "libtb_ref_actor_inputs.so")
 
 _vp = ctypes.c_void_p
 _sz = ctypes.c_size_t
@@ -180,3 +181,63 @@ def quantize_cameras(cameras_f32):
     out = np.empty(c.shape, np.uint8)
     lib().oracle_quantize_cameras(_addr(c), c.size, _addr(out))
     return out
+
+
+def actor_inputs_cpu(obs, mission, cameras, tactical, prior):
+    """CPU restatement of the reference's learner input preparation
+    (src/network/network_gpu.cu:274-303 scalar_inputs, :467-479
+    lidar_channels, :480-483 camera_luma), given the onboard tactical/prior
+    values.  float32 arithmetic; the symlog uses numpy's log1p, so it may
+    differ from the GPU's log1pf in the last bits (the other tensors are
+    exact: IEEE divisions, and the luma multiply-add evaluated exactly and
+    rounded once, as the GPU's fused multiply-add does)."""
+    n = obs.shape[0]
+    f32 = np.float32
+    raw = np.concatenate([obs[:, :48], obs[:, 4144:4148]], axis=1).astype(f32)
+    raw = np.where(np.isfinite(raw), np.clip(raw, f32(-1000), f32(1000)), f32(0)).astype(f32)
+    scale = np.ones(52, f32)
+    scale[0:3] = 0.05; scale[3:6] = 0.10; scale[10:13] = 0.20; scale[13:16] = 0.10
+    scale[28:32] = 0.50; scale[32:36] = 0.20
+    symlog = np.copysign(np.log1p(np.abs(raw * scale)).astype(f32), raw).astype(f32)
+    proprio = np.empty((n, 91), f32)
+    proprio[:, :52] = np.clip(symlog / np.sqrt(f32(1.0001)).astype(f32), f32(-8), f32(8))
+    proprio[:, 52:76] = tactical
+    proprio[:, 76:91] = prior
+    mission_vec = np.empty((n, 49), f32)
+    mission_vec[:, :10] = np.where(np.isfinite(mission), mission, f32(0))
+    mission_vec[:, 10:34] = tactical
+    mission_vec[:, 34:49] = prior
+    r = obs[:, 48:4144].reshape(n, 2, 2048).astype(f32)
+    with np.errstate(invalid="ignore"):
+        valid = (r > 0) & np.isfinite(r)
+        clamped = np.maximum(f32(0.05), np.minimum(f32(30), np.nan_to_num(r, nan=0.0))).astype(f32)
+        inverse = np.where(valid, (f32(1) / np.maximum(f32(0.2), clamped)).astype(f32), f32(0))
+        scaled = np.where(valid, (clamped / f32(30)).astype(f32), f32(1))
+    lidar = np.concatenate([inverse, scaled, valid.astype(f32)], axis=1).astype(f32)
+    k = np.float64(f32(1) / f32(255))
+    luma = (cameras.astype(np.float64) * k - 0.5).astype(f32)
+    return {"proprio": proprio, "mission": mission_vec, "lidar": lidar, "luma": luma}
+
+
+def have_reference_actor_inputs() -> bool:
+    return os.path.exists(REF_ACTOR_INPUTS_PATH)
+
+
+_ref_actor = None
+
+
+def actor_inputs_reference_gpu(d_obs, d_mission, d_cameras, outs, n: int) -> None:
+    """Run the reference's own GPU input-preparation kernels (oracle/_ref) on
+    device buffers: outs = (proprio, mission_vec, tactical, prior, lidar, luma)
+    torch tensors; synchronous."""
+    global _ref_actor
+    if _ref_actor is None:
+        l = ctypes.CDLL(REF_ACTOR_INPUTS_PATH)
+        l.tb_ref_actor_inputs.restype = ctypes.c_int
+        l.tb_ref_actor_inputs.argtypes = [_vp] * 9 + [ctypes.c_int]
+        _ref_actor = l
+    ptrs = [t.data_ptr() for t in (d_obs, d_mission, d_cameras, *outs)]
+    if not _ref_actor.tb_ref_actor_inputs(*ptrs, n):
+        raise RuntimeError("reference input-preparation launch failed")
+    import torch
+    torch.cuda.synchronize()

@@ -1,0 +1,135 @@
+"""GPU parity of tb_cuda_prepare_actor_inputs_device (the 618M learner's
+input tensors) against two oracles:
+
+ * the reference's own GPU kernels (scalar_inputs, lidar_channels,
+   camera_luma in src/network/network_gpu.cu), compiled where they lie into
+   oracle/_ref by oracle/Makefile: the LiDAR channels, luma, mission and
+   symlog proprioception must be identical bit for bit; the 39 onboard values
+   (which the reference computes with CUDA's float transcendentals and this
+   library with correctly rounded ones) within the reference test's 5e-5,
+   with identical flags;
+ * a numpy restatement (oracle.actor_inputs_cpu): exact for LiDAR, luma and
+   mission, 1e-6 + 1e-5*|ref| for the symlog values.
+The onboard slots must also equal tb_cuda_extract_onboard_device's output.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+import turbinator_c_b200 as tb
+from tests.golden import fixtures
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+FLAGS_TACTICAL = (11, 22)
+
+
+def _outputs(n):
+    z = lambda *shape: torch.full(shape, float("nan"), device="cuda")
+    return z(n, 91), z(n, 49), z(n, 24), z(n, 15), z(n, 6 * 2048), z(n, 16384)
+
+
+def run(obs, mission, cams):
+    n = obs.shape[0]
+    d = [torch.from_numpy(np.ascontiguousarray(x)).cuda() for x in (obs, mission, cams)]
+    outs = _outputs(n)
+    torch.cuda.synchronize()
+    assert tb.tb_cuda_prepare_actor_inputs_device(*d, *outs, n) == 1
+    torch.cuda.synchronize()
+    return d, [o.cpu().numpy() for o in outs]
+
+
+def check(obs, mission, cams, what):
+    d, (proprio, mvec, tac, pri, lidar, luma) = run(obs, mission, cams)
+    n = obs.shape[0]
+    for a in (proprio, mvec, tac, pri, lidar, luma):
+        assert np.isfinite(a).all(), what
+    # onboard slots are the onboard entry point's values
+    assert np.array_equal(proprio[:, 52:76], tac) and np.array_equal(proprio[:, 76:], pri)
+    assert np.array_equal(mvec[:, 10:34], tac) and np.array_equal(mvec[:, 34:], pri)
+    assert np.array_equal(np.concatenate([tac, pri], 1), oracle.onboard_reference_cr(obs, mission))
+    # numpy restatement
+    cpu = oracle.actor_inputs_cpu(obs, mission, cams, tac, pri)
+    assert np.array_equal(lidar.view(np.uint32), cpu["lidar"].reshape(n, -1).view(np.uint32)), what
+    assert np.array_equal(luma.view(np.uint32), cpu["luma"].view(np.uint32)), what
+    assert np.array_equal(mvec[:, :10].view(np.uint32), cpu["mission"][:, :10].view(np.uint32)), what
+    err = np.abs(proprio[:, :52].astype(np.float64) - cpu["proprio"][:, :52])
+    assert np.all(err <= 1e-6 + 1e-5 * np.abs(cpu["proprio"][:, :52])), what
+    # the reference's own kernels
+    if oracle.have_reference_actor_inputs():
+        ref_outs = _outputs(n)
+        oracle.actor_inputs_reference_gpu(*d, ref_outs, n)
+        rp, rm, rt, rpri, rl, rlu = [o.cpu().numpy() for o in ref_outs]
+        assert np.array_equal(lidar.view(np.uint32), rl.view(np.uint32)), what
+        assert np.array_equal(luma.view(np.uint32), rlu.view(np.uint32)), what
+        assert np.array_equal(proprio[:, :52].view(np.uint32), rp[:, :52].view(np.uint32)), what
+        assert np.array_equal(mvec[:, :10].view(np.uint32), rm[:, :10].view(np.uint32)), what
+        mine = np.concatenate([tac, pri], 1)
+        theirs = np.concatenate([rt, rpri], 1)
+        assert np.max(np.abs(mine.astype(np.float64) - theirs)) <= 5e-5, what
+        for c in FLAGS_TACTICAL + (24 + 14,):
+            assert np.array_equal(mine[:, c], theirs[:, c]), what
+
+
+def test_seeded_batch():
+    obs, mission, cams, _ = tb.generate(2, 0, 4096)
+    check(obs, mission, cams, "seeded")
+
+
+def test_stress_quarters():
+    obs, mission, cams, _ = tb.generate(4, 0, 4096, total=4096, stress=True)
+    check(obs, mission, cams, "stress")
+
+
+def test_edge_values():
+    obs, mission, cams = fixtures.edge_inputs()
+    check(obs, mission, cams, "edge")
+
+
+@pytest.mark.parametrize("n", [1, 3, 1185])
+def test_ragged_batches(n):
+    obs, mission, cams, _ = tb.generate(42, 0, n)
+    check(obs, mission, cams, f"B={n}")
+
+
+def test_argument_rejection():
+    n = 4
+    obs, mission, cams, _ = tb.generate(43, 0, n)
+    d = [torch.from_numpy(x).cuda() for x in (obs, mission, cams)]
+    outs = _outputs(n)
+    assert tb.tb_cuda_prepare_actor_inputs_device(d[0], d[1], None, *outs, n) == 0
+    assert tb.tb_cuda_prepare_actor_inputs_device(d[0], d[1], d[2], *outs, 0) == 0
+    assert tb.tb_cuda_prepare_actor_inputs_device(d[0].data_ptr() + 4, d[1], d[2], *outs, n) == 0
+
+
+@pytest.mark.skipif(not oracle.have_reference_actor_inputs(), reason="reference GPU build absent")
+def test_faster_than_the_reference_kernels():
+    """Records both timings at 65,536 aircraft (CUDA events) and requires this
+    library's single call to beat the reference's three launches."""
+    n = 65536
+    obs, mission, cams, _ = tb.generate(2, 0, n)
+    d = [torch.from_numpy(x).cuda() for x in (obs, mission, cams)]
+    outs = _outputs(n)
+    ptrs = [t.data_ptr() for t in (*d, *outs)]
+    oracle.actor_inputs_reference_gpu(*d, outs, n)   # loads the reference build
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / 10
+
+    mine = timed(lambda: tb.tb_cuda_prepare_actor_inputs_device(*d, *outs, n))
+    ref = timed(lambda: oracle._ref_actor.tb_ref_actor_inputs(*ptrs, n))
+    print(f"\nactor inputs, 65,536 aircraft: this library {mine:.3f} ms, reference kernels {ref:.3f} ms")
+    assert mine < ref

@@ -31,6 +31,10 @@ ONBOARD_DIM = 39
 BYTES_PER_SAMPLE = OBS_DIM * 4 + MISSION_DIM * 4 + CAMERA_BYTES + FEATURE_DIM * 4
 #: The same for the FP32-camera entry point (65,536 camera bytes read).
 BYTES_PER_SAMPLE_F32CAM = OBS_DIM * 4 + MISSION_DIM * 4 + 4 * CAMERA_BYTES + FEATURE_DIM * 4
+#: Learner input tensors: 33,016 bytes read; proprio 91 + mission 49 + tactical 24 + prior 15
+#: + LiDAR 6 x 2048 + luma 16,384 floats written.
+BYTES_PER_SAMPLE_ACTOR_INPUTS = (OBS_DIM * 4 + MISSION_DIM * 4 + CAMERA_BYTES +
+                                 4 * (91 + 49 + 24 + 15 + 6 * 2048 + CAMERA_BYTES))
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libturbinator_cuda.so")
@@ -81,6 +85,7 @@ def load_library() -> ctypes.CDLL:
     _bind(lib, "tb_cuda_extract_features_host_noalloc", _c.c_int, [_vp, _vp, _vp, _sz, _vp, _vp])
     _bind(lib, "tb_cuda_extract_onboard_device", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
     _bind(lib, "tb_cuda_extract_features_device_f32cam", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
+    _bind(lib, "tb_cuda_prepare_actor_inputs_device", _c.c_int, [_vp] * 9 + [_sz, _vp])
     _bind(lib, "tb_features_launch_f32cam", _c.c_int,
           [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_launch", _c.c_int,
@@ -144,6 +149,14 @@ def tb_cuda_extract_features_host(handle: Optional[int], obs, mission, cameras, 
 
 
 # ---- additive entry points ----
+
+def tb_cuda_prepare_actor_inputs_device(obs, mission, cameras, proprio_91, mission_49, tactical_24, prior_15,
+                                        lidar_6x2048, camera_luma, batch_size: int, stream=None) -> int:
+    """The 618M learner's input tensors (device pointers)."""
+    return load_library().tb_cuda_prepare_actor_inputs_device(
+        _ptr(obs), _ptr(mission), _ptr(cameras), _ptr(proprio_91), _ptr(mission_49), _ptr(tactical_24),
+        _ptr(prior_15), _ptr(lidar_6x2048), _ptr(camera_luma), batch_size, _stream_handle(stream))
+
 
 def tb_cuda_extract_features_device_f32cam(obs, mission, cameras_f32, features, batch_size: int,
                                            stream=None) -> int:
