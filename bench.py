@@ -46,6 +46,8 @@ BATCH_PER_GPU = 65536
 SEED = 2
 FALLBACK_HBM_GBS = 6650.0
 PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "features_staged_kernel_traffic.txt")
+SENSOR_SCENES = 32768
+RAYS_PER_SCENE = 4096 + 16384
 
 
 def parse_args():
@@ -61,6 +63,8 @@ def parse_args():
     p.add_argument("--no-onboard", action="store_true", help="skip the onboard tactical/prior leg")
     p.add_argument("--no-f32cam", action="store_true", help="skip the FP32-camera entry-point leg")
     p.add_argument("--no-actor-inputs", action="store_true", help="skip the learner-input leg")
+    p.add_argument("--no-sensors", action="store_true", help="skip the sensor-rendering leg")
+    p.add_argument("--sensor-scenes", type=int, default=SENSOR_SCENES, help="scenes per GPU in the sensor leg")
     return p.parse_args()
 
 
@@ -255,6 +259,65 @@ def time_onboard_reference_cpu(obs, mission, target_s: float):
                       f"{t:.2f} s wall"}
 
 
+def time_sensors(scenes, steps, warmup, stream, dev):
+    """Device time per launch of tb_cuda_render_sensors_device over the
+    resident scenes (LiDAR, valid fractions and cameras of every scene), and
+    the same call end to end: page-locked scenes copied in and every output
+    copied back inside each step, on the same stream, host wall clock."""
+    import torch
+
+    from turbinator_c_b200.sensors import tb_cuda_render_sensors_device as render
+
+    n = len(scenes)
+    h_scenes = torch.from_numpy(scenes.view(np.uint8).reshape(-1).copy()).pin_memory()
+    d_scenes = h_scenes.to(dev)
+    lidar = torch.empty((n, 4096), dtype=torch.float32, device=dev)
+    valid = torch.empty((n, 2), dtype=torch.float32, device=dev)
+    cams = torch.empty((n, 16384), dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize(dev)
+    for _ in range(max(warmup, 3)):
+        assert render(d_scenes, n, lidar, 4096, valid, 2, cams, None, stream) == 1
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        render(d_scenes, n, lidar, 4096, valid, 2, cams, None, stream)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    per_launch = start.elapsed_time(end) / 1e3 / steps
+    h_lidar = torch.empty((n, 4096), dtype=torch.float32, pin_memory=True)
+    h_valid = torch.empty((n, 2), dtype=torch.float32, pin_memory=True)
+    h_cams = torch.empty((n, 16384), dtype=torch.uint8, pin_memory=True)
+    e2e_steps = max(1, min(steps, 5))
+    with torch.cuda.stream(stream):
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            d_scenes.copy_(h_scenes, non_blocking=True)
+            render(d_scenes, n, lidar, 4096, valid, 2, cams, None, stream)
+            h_lidar.copy_(lidar, non_blocking=True)
+            h_valid.copy_(valid, non_blocking=True)
+            h_cams.copy_(cams, non_blocking=True)
+            stream.synchronize()
+        e2e = (time.perf_counter() - t0) / e2e_steps
+    if not np.isfinite(h_valid.numpy()).all():
+        raise RuntimeError("non-finite LiDAR valid fractions")
+    return per_launch, e2e, n * (4096 * 4 + 8 + 16384)
+
+
+def time_sensors_reference_cpu(scenes, target_s: float):
+    import oracle  # test infrastructure: the CPU baseline only
+
+    threads = host_threads()
+    n = len(scenes)
+    probe = min(n, max(threads * 2, 64))
+    rate = probe / max(oracle.timed_sensors_reference(scenes[:probe], threads), 1e-9)
+    sample = int(min(n, max(probe, rate * target_s)))
+    t = oracle.timed_sensors_reference(scenes[:sample], threads)
+    return {"value": sample / t, "unit": "scenes/s", "cores": threads, "kind": "reference",
+            "sample": f"first {sample} scenes, the reference simulator's tb_sim_render_lidar + "
+                      f"tb_sim_render_camera (oracle/_ref, ISO C11 -O2), {threads} threads, {t:.2f} s wall"}
+
+
 # ---------------------------------------------------------------- arms
 
 def run_reference_arm(args, rank: int, world: int):
@@ -432,6 +495,39 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                    "bound": "SM instruction issue (control law + LiDAR scans), not HBM", **legs,
                    "launches": 2 * args.steps}
 
+    # ---- simulator sensor rendering (tb_cuda_render_sensors_device), its own scenes
+    sensors = None
+    sensor_scene_sets = {}
+    if not args.no_sensors:
+        from turbinator_c_b200.sensors import synthetic_scenes
+
+        legs = {}
+        for name, balls in (("flight_mix", "flight"), ("heaviest", "max")):
+            # weak scaling: each rank renders its own seeded scenes
+            scount = args.sensor_scenes
+            total_s = scount * world
+            scenes = synthetic_scenes(SEED * 1000 + rank, scount, balls=balls)
+            sensor_scene_sets[name] = scenes
+            s_steps = max(1, min(args.steps, 10))
+            per, e2e_per, d2h = time_sensors(scenes, s_steps, args.warmup, stream, dev)
+            per_max, e2e_max = max_over_ranks(per), max_over_ranks(e2e_per)
+            legs[name] = {"value": total_s / per_max, "unit": "scenes/s", "ms_per_launch": per_max * 1e3,
+                          "rays_per_s": total_s * RAYS_PER_SCENE / per_max, "scenes_per_gpu": scount,
+                          "mean_spheres_per_scene": float(np.mean(
+                              np.clip(scenes["obstacle_count"], 0, 24) + np.clip(scenes["ball_count"], 0, 64))),
+                          "e2e": {"value": total_s / e2e_max, "unit": "scenes/s", "ms_per_step": e2e_max * 1e3,
+                                  "h2d_bytes_per_step": scount * 2432, "d2h_bytes_per_step": d2h,
+                                  "api": "scenes copied in from page-locked memory, LiDAR + valid + cameras "
+                                         "copied back, every step (host wall clock)"},
+                          "launches": s_steps + max(1, min(s_steps, 5))}
+        sensors = {"entry_point": "tb_cuda_render_sensors_device",
+                   "outputs": "4,096 LiDAR ranges + 2 valid fractions + 4 x 64 x 64 camera bytes per scene",
+                   "bound": "FP64 pipe (double-precision ray/sphere tests, no FMA contraction), not HBM",
+                   "data": "synthetic scenes with the simulator's geometry (seeded); flight_mix: uniform over "
+                           "the 28 scenarios, 0-12 cannon balls in arena scenes; heaviest: 24 obstacles in "
+                           "every course scene and 64 balls in every arena scene",
+                   **legs, "launches": sum(v["launches"] for v in legs.values())}
+
     # ---- e2e: the reference-facing host ABI on page-locked host buffers
     e2e_steps = args.e2e_steps or min(args.steps, 20)
     out_host = torch.empty((count, 142), dtype=torch.float32, pin_memory=True).numpy()
@@ -509,11 +605,13 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                      "algorithmic_bytes_per_launch": count * tb.BYTES_PER_SAMPLE,
                      "kernel": "features_staged_kernel", "avg_launch_ms": avg_launch_s * 1e3},
         "gpu_launches": (args.steps + e2e_steps * chunks + (onboard["launches"] if onboard else 0) +
-                         (f32cam["launches"] if f32cam else 0) + (actor["launches"] if actor else 0)),
+                         (f32cam["launches"] if f32cam else 0) + (actor["launches"] if actor else 0) +
+                         (sensors["launches"] if sensors else 0)),
         "gpu_launches_detail": {"value_region": args.steps, "e2e_region": e2e_steps * chunks,
                                 "onboard_regions": onboard["launches"] if onboard else 0,
                                 "f32cam_region": f32cam["launches"] if f32cam else 0,
-                                "actor_inputs_region": actor["launches"] if actor else 0},
+                                "actor_inputs_region": actor["launches"] if actor else 0,
+                                "sensors_regions": sensors["launches"] if sensors else 0},
         "clocks": clk,
     }
     if f32cam is not None:
@@ -522,10 +620,18 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         line["actor_inputs"] = actor
     if onboard is not None:
         line["onboard"] = onboard
+    if sensors is not None:
+        line["sensors"] = sensors
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = time_reference_cpu(obs, mission, cams, args.cpu_seconds)
         if onboard is not None:
             onboard["cpu_baseline"] = time_onboard_reference_cpu(obs, mission, args.cpu_seconds / 2)
+        if sensors is not None:
+            import oracle  # test infrastructure: the CPU baseline only
+
+            if oracle.have_reference_sensors():
+                for name, scenes in sensor_scene_sets.items():
+                    sensors[name]["cpu_baseline"] = time_sensors_reference_cpu(scenes, args.cpu_seconds / 2)
     print(json.dumps(line), flush=True)
 
 

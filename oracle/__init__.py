@@ -241,3 +241,111 @@ def actor_inputs_reference_gpu(d_obs, d_mission, d_cameras, outs, n: int) -> Non
         raise RuntimeError("reference input-preparation launch failed")
     import torch
     torch.cuda.synchronize()
+
+
+# ---- sensor rendering (tb_cuda_render_sensors_device's checker) ----
+
+REF_SENSORS_PATH = os.path.join(HERE, "_ref", "libtb_ref_sensors.so")
+_ref_sensors = None
+_sensor_port_bound = False
+
+
+def _sensor_port() -> ctypes.CDLL:
+    global _sensor_port_bound
+    l = lib()
+    if not _sensor_port_bound:
+        l.oracle_render_sensors.restype = None
+        l.oracle_render_sensors.argtypes = [_vp, ctypes.c_int64, _vp, ctypes.c_int64, _vp, ctypes.c_int64, _vp, _vp]
+        l.oracle_sensor_scene_layout.restype = None
+        l.oracle_sensor_scene_layout.argtypes = [_vp]
+        _sensor_port_bound = True
+    return l
+
+
+def have_reference_sensors() -> bool:
+    return os.path.exists(REF_SENSORS_PATH)
+
+
+def ref_sensors() -> ctypes.CDLL:
+    global _ref_sensors
+    if _ref_sensors is None:
+        if not have_reference_sensors():
+            raise RuntimeError(f"{REF_SENSORS_PATH} missing (reference build not available)")
+        l = ctypes.CDLL(REF_SENSORS_PATH)
+        l.ref_sensors_render.restype = ctypes.c_double
+        l.ref_sensors_render.argtypes = [_vp, ctypes.c_int64, _vp, ctypes.c_int64, _vp, ctypes.c_int64, _vp, _vp,
+                                         ctypes.c_int]
+        l.ref_sensors_simulate.restype = ctypes.c_int
+        l.ref_sensors_simulate.argtypes = [ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]
+        _ref_sensors = l
+    return _ref_sensors
+
+
+def sensor_scene_layout():
+    """(sizeof, offsets of the 14 fields) of tb_sensor_scene as C lays it out."""
+    out = np.zeros(15, np.int64)
+    _sensor_port().oracle_sensor_scene_layout(_addr(out))
+    return out
+
+
+def _sensor_outputs(n: int, raw: bool):
+    lidar = np.full((n, 4096), np.nan, np.float32)
+    valid = np.full((n, 2), np.nan, np.float32)
+    cams = np.zeros((n, 16384), np.uint8)
+    raws = np.zeros((n, 147456), np.uint8) if raw else None
+    return lidar, valid, cams, raws
+
+
+def render_sensors_port(scenes, raw: bool = False):
+    """Restated renderers (sensors_oracle.c): (lidar [n,4096], valid [n,2],
+    cameras [n,16384], raw [n,147456] or None); unrendered rows keep NaN / 0."""
+    scenes = np.ascontiguousarray(scenes)
+    n = scenes.shape[0]
+    lidar, valid, cams, raws = _sensor_outputs(n, raw)
+    _sensor_port().oracle_render_sensors(_addr(scenes), n, _addr(lidar), 4096, _addr(valid), 2, _addr(cams),
+                                         _addr(raws))
+    return lidar, valid, cams, raws
+
+
+def render_sensors_reference(scenes, raw: bool = False, threads: int = 0):
+    """The reference simulator's own renderers on the same scenes (same
+    outputs as render_sensors_port)."""
+    scenes = np.ascontiguousarray(scenes)
+    n = scenes.shape[0]
+    lidar, valid, cams, raws = _sensor_outputs(n, raw)
+    t = ref_sensors().ref_sensors_render(_addr(scenes), n, _addr(lidar), 4096, _addr(valid), 2, _addr(cams),
+                                         _addr(raws), threads or min(os.cpu_count() or 1, 64))
+    if t < 0:
+        raise RuntimeError("reference sensor renderer failed")
+    return lidar, valid, cams, raws
+
+
+def timed_sensors_reference(scenes, threads: int) -> float:
+    """Wall seconds for the reference renderers over the scenes on `threads`
+    host threads (LiDAR, valid fractions and cameras)."""
+    scenes = np.ascontiguousarray(scenes)
+    n = scenes.shape[0]
+    lidar, valid, cams, _ = _sensor_outputs(n, False)
+    t = ref_sensors().ref_sensors_render(_addr(scenes), n, _addr(lidar), 4096, _addr(valid), 2, _addr(cams), None,
+                                         threads)
+    if t < 0:
+        raise RuntimeError("reference sensor renderer failed")
+    return t
+
+
+def simulate_sensor_scenes(scenarios, seeds, steps, players, scene_dtype):
+    """Scenes packed from simulated episodes plus the reference's renders of
+    those environments: (scenes, lidar, valid, cameras)."""
+    n = len(scenarios)
+    sc = np.ascontiguousarray(scenarios, np.int32)
+    sd = np.ascontiguousarray(seeds, np.uint64)
+    st = np.ascontiguousarray(steps, np.int32)
+    pl = np.ascontiguousarray(players, np.int32)
+    scenes = np.zeros(n, scene_dtype)
+    lidar = np.empty((n, 4096), np.float32)
+    valid = np.empty((n, 2), np.float32)
+    cams = np.empty((n, 16384), np.uint8)
+    if ref_sensors().ref_sensors_simulate(n, _addr(sc), _addr(sd), _addr(st), _addr(pl), _addr(scenes),
+                                          _addr(lidar), _addr(valid), _addr(cams)) != 0:
+        raise RuntimeError("reference simulation failed")
+    return scenes, lidar, valid, cams

@@ -44,6 +44,16 @@ def test_argument_rejection_without_device():
     assert tb.tb_cuda_extract_features_host(None, fake, fake, fake, 1, fake) == 0
     assert tb.tb_cuda_feature_batch_create(0, 0) is None
     tb.tb_cuda_feature_batch_destroy(None)  # NULL-safe
+    from turbinator_c_b200.sensors import tb_cuda_render_sensors_device as render
+    assert render(None, 4, fake, 4096, fake, 2, fake) == 0
+    assert render(fake, 0, fake, 4096, fake, 2, fake) == 0
+    assert render(fake, 0x80000000, fake, 4096, fake, 2, fake) == 0
+    assert render(fake + 4, 4, fake, 4096, fake, 2, fake) == 0        # scenes not 8-byte aligned
+    assert render(fake, 4, fake, 4095, fake, 2, fake) == 0            # LiDAR stride below 4096
+    assert render(fake, 4, fake, 4096, fake, 1, fake) == 0            # valid stride below 2
+    assert render(fake, 4, fake + 2, 4096, fake, 2, fake) == 0        # misaligned LiDAR
+    assert render(fake, 4, fake, 4096, fake, 2, fake + 1) == 0        # misaligned cameras
+    assert render(fake, 4, fake, 4096, fake, 2, fake, fake + 2) == 0  # misaligned raw capture
 
 
 def test_library_is_sm100a_only_build():

@@ -86,6 +86,7 @@ def load_library() -> ctypes.CDLL:
     _bind(lib, "tb_cuda_extract_onboard_device", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
     _bind(lib, "tb_cuda_extract_features_device_f32cam", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
     _bind(lib, "tb_cuda_prepare_actor_inputs_device", _c.c_int, [_vp] * 9 + [_sz, _vp])
+    _bind(lib, "tb_cuda_render_sensors_device", _c.c_int, [_vp, _sz, _vp, _sz, _vp, _sz, _vp, _vp, _vp])
     _bind(lib, "tb_features_launch_f32cam", _c.c_int,
           [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_launch", _c.c_int,

@@ -1,0 +1,419 @@
+/*
+ * sm_100a ray tracer for the simulator's sensors: per scene the 2 x 2,048
+ * LiDAR rays and the 4 x 4,096 camera rays, for a batch of scenes in one
+ * launch (tb_cuda_render_sensors_device, include/turbinator/sim/cuda_sensors.h).
+ *
+ * Reference (Viatreen/Turbinator_C src/sim/sensors.c):
+ *   sphere_hit :4-10, trace :11-26, tb_sim_render_lidar :28-50,
+ *   camera_ray :52-58, shade :59-68, tb_sim_render_camera :69-82;
+ *   helpers tb_rotate / tb_clamp / tb_is_arena / tb_is_bwb, sim_internal.h:73-88;
+ *   tb_rand64 (SplitMix64), physics.c:73-78.
+ *
+ * Design (B200):
+ *  - Work unit = 2,048 rays of one scene: LiDAR head 0 or 1, or one half
+ *    (32 rows) of one camera view -- 10 units per scene, one 256-thread CTA
+ *    per unit, CTAs striding over units.  Each unit traces from a single
+ *    origin, so the ray-independent sphere terms (o - c, |o - c|^2, r^2) and
+ *    the dome's constant term are formed once per CTA in shared memory and
+ *    read as warp broadcasts.
+ *  - Body-frame ray directions do not depend on the scene: they are built on
+ *    the host with the C library the simulator uses (sensor_rays.c) and read
+ *    from global memory (SoA, coalesced); the kernel only rotates them.
+ *  - The LiDAR noise stream is SplitMix64, whose state after k draws is
+ *    seed + k * golden, so ray k hashes its own state without a sequential
+ *    pass.
+ *  - Everything is evaluated in double precision with the simulator's
+ *    expression order and no multiply-add contraction (this file is built
+ *    with -fmad=false); double division and square root are correctly
+ *    rounded, so ranges equal the simulator's bit for bit.  The only
+ *    transcendental per ray is the camera's exp(-d/80).
+ *  - Camera bytes are written four pixels per 32-bit store (a warp covers 128
+ *    contiguous bytes); the optional raw capture writes each pixel 3 x 3.
+ *  The work is FP64-pipe bound (no tensor-core or HBM bound applies): about
+ *  35 double operations to rotate a ray plus about 8 per sphere tested.
+ */
+#include <cuda_runtime.h>
+
+#include <math.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "tb_sensor_rays.h"
+#include "turbinator/sim/cuda_sensors.h"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnitRays = 2048;
+constexpr int kUnitsPerScene = 10; /* 2 LiDAR heads + 4 views x 2 halves */
+constexpr int kMaxSpheres = TB_SENSOR_MAX_OBSTACLES + 1 + TB_SENSOR_MAX_BALLS;
+constexpr int kLidarBins = TB_SENSOR_LIDAR_BINS;
+constexpr int kCameraPixels = TB_SENSOR_CAMERA_PIXELS;
+constexpr unsigned long long kGolden = 0x9e3779b97f4a7c15ull;
+
+static_assert(sizeof(tb_sensor_scene) == 2432, "scene record layout");
+
+/* Body-frame directions, structure of arrays. */
+__device__ double g_lidar_x[kLidarBins], g_lidar_y[kLidarBins], g_lidar_z[kLidarBins];
+__device__ unsigned int g_lidar_blocked[kLidarBins / 32];
+__device__ double g_camera_x[kCameraPixels], g_camera_y[kCameraPixels], g_camera_z[kCameraPixels];
+
+struct Vec {
+    double x, y, z;
+};
+
+/* tb_rotate (sim_internal.h:85): v + 2w(u x v) + u x (2(u x v)). */
+__device__ __forceinline__ Vec rotate(double qw, double qx, double qy, double qz, Vec v) {
+    const Vec c = {qy * v.z - qz * v.y, qz * v.x - qx * v.z, qx * v.y - qy * v.x};
+    const Vec t = {c.x * 2, c.y * 2, c.z * 2};
+    const Vec a = {v.x + t.x * qw, v.y + t.y * qw, v.z + t.z * qw};
+    return Vec{a.x + (qy * t.z - qz * t.y), a.y + (qz * t.x - qx * t.z), a.z + (qx * t.y - qy * t.x)};
+}
+
+__device__ __forceinline__ bool is_bwb(int s) { return s >= 22 && s <= 27; }
+__device__ __forceinline__ bool is_arena(int s) {
+    return s == 3 || s == 14 || s == 15 || s == 16 || s == 18 || s == 22 || s == 24 || s == 27;
+}
+
+/* One unit's scene, prepared for tracing from one origin. */
+struct UnitScene {
+    double ocx[kMaxSpheres], ocy[kMaxSpheres], ocz[kMaxSpheres]; /* origin - centre */
+    double occ[kMaxSpheres];                                     /* |origin - centre|^2 */
+    double rr[kMaxSpheres];                                      /* radius^2 */
+    double q[4];
+    double origin[3];
+    double best0;     /* trace()'s starting distance (also the sky distance) */
+    double max_range; /* LiDAR clamp */
+    double dome_cc;   /* o.x^2 + o.y^2 - dome^2 */
+    unsigned long long seed;
+    int obstacles, opponent, balls; /* sphere counts, in trace order */
+    int shelf;                      /* scenario 10's raised ground at z = 9, x >= 20 */
+    int skip;                       /* this unit renders nothing */
+    int valid[kThreads / 32];
+};
+
+/* sphere_hit (sensors.c:4-10) with the ray-independent terms precomputed in
+ * the same rounding: b = oc.d, disc = (b*b - oc.oc) + r*r. */
+__device__ __forceinline__ double sphere_hit(const UnitScene &s, int i, Vec d) {
+    const double b = s.ocx[i] * d.x + s.ocy[i] * d.y + s.ocz[i] * d.z;
+    const double disc = b * b - s.occ[i] + s.rr[i];
+    if (disc < 0) return INFINITY;
+    const double root = sqrt(disc);
+    double t = -b - root;
+    if (t <= 0.05) t = -b + root;
+    return t > 0.05 ? t : INFINITY;
+}
+
+/* trace (sensors.c:11-26): nearest hit along d from the unit's origin, in the
+ * simulator's test order (ground, shelf, obstacles, opponent, dome, balls);
+ * kind -1 sky, 0 ground, 1 obstacle, 2 opponent, 3 dome, 4 ball. */
+__device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
+    double best = s.best0;
+    kind = -1;
+    const double ox = s.origin[0], oy = s.origin[1], oz = s.origin[2];
+    if (d.z < -1e-5) {
+        const double t = (0 - oz) / d.z;
+        if (t > 0.05 && t < best) {
+            best = t;
+            kind = 0;
+        }
+        if (s.shelf) {
+            const double t2 = (9 - oz) / d.z;
+            if (t2 > 0.05 && t2 < best && ox + t2 * d.x >= 20) {
+                best = t2;
+                kind = 0;
+            }
+        }
+    }
+    int i = 0;
+    for (; i < s.obstacles; ++i) {
+        const double t = sphere_hit(s, i, d);
+        if (t < best) {
+            best = t;
+            kind = 1;
+        }
+    }
+    if (s.opponent) {
+        const double t = sphere_hit(s, i, d);
+        if (t < best) {
+            best = t;
+            kind = 2;
+        }
+        ++i;
+        const double a = d.x * d.x + d.y * d.y, b = 2 * (ox * d.x + oy * d.y);
+        const double disc = b * b - 4 * a * s.dome_cc;
+        if (a > 1e-9 && disc >= 0) {
+            const double td = (-b + sqrt(disc)) / (2 * a);
+            if (td > 0.05 && td < best) {
+                best = td;
+                kind = 3;
+            }
+        }
+    }
+    const int end = i + s.balls;
+    for (; i < end; ++i) {
+        const double t = sphere_hit(s, i, d);
+        if (t < best) {
+            best = t;
+            kind = 4;
+        }
+    }
+    return best;
+}
+
+/* shade (sensors.c:59-68). */
+__device__ __forceinline__ uint32_t shade(double distance, int kind, double dz) {
+    double luma = 0.22 + 0.15 * fmax(-1.0, fmin(1.0, dz));
+    if (kind == 0) luma = 0.28 + 0.17 * fmax(0.0, fmin(1.0, -dz));
+    if (kind == 1) luma = 0.65;
+    if (kind == 2) luma = 0.90;
+    if (kind == 3) luma = 0.46;
+    if (kind == 4) luma = 1.0;
+    luma *= 0.75 + 0.25 * exp(-distance / 80);
+    return static_cast<uint32_t>(fmax(0.0, fmin(255.0, round(luma * 255))));
+}
+
+__device__ __forceinline__ unsigned long long splitmix(unsigned long long z) {
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+/* Loads the unit's scene and forms its per-origin terms (all threads). */
+__device__ void prepare_unit(UnitScene &s, const tb_sensor_scene *__restrict__ scene, int part, bool lidar_out,
+                             bool camera_out) {
+    const int t = threadIdx.x;
+    if (t == 0) {
+        const int sensors = scene->sensors;
+        const bool want = part < 2 ? (lidar_out && (sensors & TB_SENSOR_LIDAR))
+                                   : (camera_out && (sensors & TB_SENSOR_CAMERA));
+        s.skip = !want;
+        const int scenario = scene->scenario;
+        const bool bwb = is_bwb(scenario), arena = is_arena(scenario);
+        const double qw = scene->attitude[0], qx = scene->attitude[1], qy = scene->attitude[2],
+                     qz = scene->attitude[3];
+        s.q[0] = qw;
+        s.q[1] = qx;
+        s.q[2] = qy;
+        s.q[3] = qz;
+        /* Sensor mounts: LiDAR heads sensors.c:32, cameras :72. */
+        Vec mount;
+        if (part < 2) {
+            mount = Vec{0.4, 0.4, part ? -0.4 : 0.4};
+        } else {
+            const int view = (part - 2) >> 1;
+            mount = view < 2 ? Vec{0.42, 0.42, view == 0 ? 0.13 : 0.08} : Vec{0, 0, view == 2 ? -0.5 : 0.5};
+        }
+        const Vec r = rotate(qw, qx, qy, qz, mount);
+        const double ox = scene->position[0] + r.x, oy = scene->position[1] + r.y, oz = scene->position[2] + r.z;
+        s.origin[0] = ox;
+        s.origin[1] = oy;
+        s.origin[2] = oz;
+        const double lidar_max = scene->lidar_max;
+        s.best0 = bwb ? fmax(lidar_max, 120.0) : lidar_max;
+        s.max_range = bwb ? fmax(120.0, lidar_max) : lidar_max;
+        const double dome = bwb ? 300.0 : scene->dome_radius;
+        s.dome_cc = ox * ox + oy * oy - dome * dome;
+        s.shelf = scenario == 10;
+        s.obstacles = min(max(scene->obstacle_count, 0), TB_SENSOR_MAX_OBSTACLES);
+        s.opponent = arena;
+        s.balls = min(max(scene->ball_count, 0), TB_SENSOR_MAX_BALLS);
+        /* sensors.c:30: rng ^ step_index * golden ^ player * 257 */
+        s.seed = scene->rng ^ (static_cast<unsigned long long>(static_cast<long long>(scene->step_index)) * kGolden) ^
+                 static_cast<unsigned long long>(static_cast<long long>(scene->player) * 257);
+    }
+    __syncthreads();
+    if (s.skip) return;
+    const int n = s.obstacles + s.opponent + s.balls;
+    if (t < n) {
+        double cx, cy, cz, radius;
+        if (t < s.obstacles) {
+            cx = scene->obstacles[t][0];
+            cy = scene->obstacles[t][1];
+            cz = scene->obstacles[t][2];
+            radius = scene->obstacles[t][3];
+        } else if (s.opponent && t == s.obstacles) {
+            cx = scene->opponent[0];
+            cy = scene->opponent[1];
+            cz = scene->opponent[2];
+            radius = is_bwb(scene->scenario) ? 0.75 : 0.45;
+        } else {
+            const int j = t - s.obstacles - s.opponent;
+            cx = scene->balls[j][0];
+            cy = scene->balls[j][1];
+            cz = scene->balls[j][2];
+            radius = 0.25;
+        }
+        const double ocx = s.origin[0] - cx, ocy = s.origin[1] - cy, ocz = s.origin[2] - cz;
+        s.ocx[t] = ocx;
+        s.ocy[t] = ocy;
+        s.ocz[t] = ocz;
+        s.occ[t] = ocx * ocx + ocy * ocy + ocz * ocz;
+        s.rr[t] = radius * radius;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) sensors_kernel(const tb_sensor_scene *__restrict__ scenes,
+                                                           unsigned long long units, float *__restrict__ lidar,
+                                                           unsigned long long lidar_stride,
+                                                           float *__restrict__ lidar_valid,
+                                                           unsigned long long valid_stride,
+                                                           unsigned char *__restrict__ cameras,
+                                                           unsigned char *__restrict__ raw) {
+    __shared__ UnitScene s;
+    const int t = threadIdx.x;
+    for (unsigned long long unit = blockIdx.x; unit < units; unit += gridDim.x) {
+        const unsigned long long scene_index = unit / kUnitsPerScene;
+        const int part = static_cast<int>(unit - scene_index * kUnitsPerScene);
+        __syncthreads(); /* the previous unit is done with s */
+        prepare_unit(s, scenes + scene_index, part, lidar != nullptr, cameras != nullptr || raw != nullptr);
+        if (s.skip) continue; /* CTA-uniform */
+        __syncthreads();
+        const double qw = s.q[0], qx = s.q[1], qy = s.q[2], qz = s.q[3];
+
+        if (part < 2) {
+            /* LiDAR head `part` (sensors.c:31-49). */
+            float *out = lidar + scene_index * lidar_stride;
+            int valid = 0;
+#pragma unroll 1
+            for (int k = 0; k < kUnitRays / kThreads; ++k) {
+                const int bin = part * kUnitRays + k * kThreads + t;
+                const unsigned long long hash = splitmix(s.seed + static_cast<unsigned long long>(bin + 1) * kGolden);
+                const bool blocked = (g_lidar_blocked[bin >> 5] >> (bin & 31)) & 1u;
+                float value = -1.0f;
+                if (!(static_cast<double>(hash & 0xffff) / 65536.0 < 0.005 || blocked)) {
+                    const Vec rw = rotate(qw, qx, qy, qz, Vec{g_lidar_x[bin], g_lidar_y[bin], g_lidar_z[bin]});
+                    int kind;
+                    double range = trace(s, rw, kind);
+                    const double noise = (static_cast<double>((hash >> 16) & 0xffff) / 32768.0 - 1.0) * 0.02;
+                    range = fmax(0.05, fmin(s.max_range, range + noise));
+                    value = static_cast<float>(range);
+                    ++valid;
+                }
+                out[bin] = value;
+            }
+            if (lidar_valid) {
+                valid = __reduce_add_sync(0xffffffffu, valid);
+                if ((t & 31) == 0) s.valid[t >> 5] = valid;
+                __syncthreads();
+                if (t == 0) {
+                    int total = 0;
+                    for (int w = 0; w < kThreads / 32; ++w) total += s.valid[w];
+                    lidar_valid[scene_index * valid_stride + part] = static_cast<float>(total) / 2048;
+                }
+            }
+        } else {
+            /* Half of camera view (part-2)/2 (sensors.c:71-79): 32 rows of 64. */
+            const int view = (part - 2) >> 1, half = (part - 2) & 1;
+#pragma unroll 1
+            for (int k = 0; k < kUnitRays / (4 * kThreads); ++k) {
+                const int local = half * kUnitRays + k * 4 * kThreads + 4 * t; /* pixel in the view */
+                const int pixel = view * 4096 + local;
+                uint32_t word = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const Vec dir = rotate(qw, qx, qy, qz,
+                                           Vec{g_camera_x[pixel + j], g_camera_y[pixel + j], g_camera_z[pixel + j]});
+                    int kind;
+                    const double d = trace(s, dir, kind);
+                    word |= shade(d, kind, dir.z) << (8 * j);
+                }
+                if (cameras)
+                    *reinterpret_cast<uint32_t *>(cameras + scene_index * kCameraPixels + pixel) = word;
+                if (raw) {
+                    /* each pixel as a 3 x 3 block of the 192 x 192 view (sensors.c:78) */
+                    const uint32_t p0 = word & 255u, p1 = (word >> 8) & 255u, p2 = (word >> 16) & 255u,
+                                   p3 = word >> 24;
+                    const uint32_t w0 = p0 | p0 << 8 | p0 << 16 | p1 << 24;
+                    const uint32_t w1 = p1 | p1 << 8 | p2 << 16 | p2 << 24;
+                    const uint32_t w2 = p2 | p3 << 8 | p3 << 16 | p3 << 24;
+                    const int y = local >> 6, x = local & 63;
+                    unsigned char *base = raw + scene_index * static_cast<unsigned long long>(TB_SENSOR_CAMERA_RAW_PIXELS) +
+                                          view * 36864 + 3 * x;
+#pragma unroll
+                    for (int dy = 0; dy < 3; ++dy) {
+                        uint32_t *row = reinterpret_cast<uint32_t *>(base + (3 * y + dy) * 192);
+                        row[0] = w0;
+                        row[1] = w1;
+                        row[2] = w2;
+                    }
+                }
+            }
+        }
+    }
+}
+
+constexpr int kMaxDevices = 64;
+bool g_tables_ready[kMaxDevices];
+int g_grid_cap[kMaxDevices];
+std::mutex g_tables_mutex;
+
+/* Uploads the body-frame ray tables to the current device (once). */
+bool ensure_tables(int dev) {
+    std::lock_guard<std::mutex> lock(g_tables_mutex);
+    if (g_tables_ready[dev]) return true;
+    static double lidar_dirs[3 * kLidarBins], camera_dirs[3 * kCameraPixels];
+    static unsigned char blocked[kLidarBins];
+    static bool built = false;
+    static double lx[kLidarBins], ly[kLidarBins], lz[kLidarBins];
+    static double cx[kCameraPixels], cy[kCameraPixels], cz[kCameraPixels];
+    static unsigned int mask[kLidarBins / 32];
+    if (!built) {
+        tb_sensor_lidar_rays(lidar_dirs, blocked);
+        tb_sensor_camera_rays(camera_dirs);
+        for (int i = 0; i < kLidarBins; ++i) {
+            lx[i] = lidar_dirs[3 * i];
+            ly[i] = lidar_dirs[3 * i + 1];
+            lz[i] = lidar_dirs[3 * i + 2];
+            if (blocked[i]) mask[i >> 5] |= 1u << (i & 31);
+        }
+        for (int i = 0; i < kCameraPixels; ++i) {
+            cx[i] = camera_dirs[3 * i];
+            cy[i] = camera_dirs[3 * i + 1];
+            cz[i] = camera_dirs[3 * i + 2];
+        }
+        built = true;
+    }
+    int sms = 0, blocks = 0;
+    if (cudaMemcpyToSymbol(g_lidar_x, lx, sizeof lx) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_lidar_y, ly, sizeof ly) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_lidar_z, lz, sizeof lz) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_lidar_blocked, mask, sizeof mask) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_camera_x, cx, sizeof cx) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_camera_y, cy, sizeof cy) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_camera_z, cz, sizeof cz) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, sensors_kernel, kThreads, 0) != cudaSuccess)
+        return false;
+    /* enough CTAs for many waves; each strides over the units */
+    g_grid_cap[dev] = sms * (blocks > 0 ? blocks : 1) * 64;
+    g_tables_ready[dev] = true;
+    return true;
+}
+
+bool aligned(const void *p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0; }
+
+} /* namespace */
+
+extern "C" int tb_cuda_render_sensors_device(const tb_sensor_scene *device_scenes, size_t count, float *device_lidar,
+                                             size_t lidar_stride, float *device_lidar_valid, size_t valid_stride,
+                                             unsigned char *device_cameras, unsigned char *device_raw_cameras,
+                                             void *stream) {
+    if (!device_scenes || count == 0 || count > 0x7fffffffu || !aligned(device_scenes, 8)) return 0;
+    if (device_lidar && (!aligned(device_lidar, 4) || lidar_stride < static_cast<size_t>(kLidarBins))) return 0;
+    if (device_lidar_valid && (!aligned(device_lidar_valid, 4) || valid_stride < 2)) return 0;
+    if ((device_cameras && !aligned(device_cameras, 4)) || (device_raw_cameras && !aligned(device_raw_cameras, 4)))
+        return 0;
+    if (!device_lidar) device_lidar_valid = nullptr;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+    if (!ensure_tables(dev)) return 0;
+    cudaGetLastError(); /* report this launch only */
+    const unsigned long long units = static_cast<unsigned long long>(count) * kUnitsPerScene;
+    const unsigned long long grid = units < static_cast<unsigned long long>(g_grid_cap[dev]) ? units : g_grid_cap[dev];
+    sensors_kernel<<<static_cast<unsigned int>(grid), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        device_scenes, units, device_lidar, lidar_stride, device_lidar_valid, valid_stride, device_cameras,
+        device_raw_cameras);
+    return cudaGetLastError() == cudaSuccess;
+}
