@@ -11,11 +11,22 @@
  *
  * Design (B200):
  *  - Work unit = 2,048 rays of one scene: LiDAR head 0 or 1, or one half
- *    (32 rows) of one camera view -- 10 units per scene, one 256-thread CTA
- *    per unit, CTAs striding over units.  Each unit traces from a single
- *    origin, so the ray-independent sphere terms (o - c, |o - c|^2, r^2) and
- *    the dome's constant term are formed once per CTA in shared memory and
- *    read as warp broadcasts.
+ *    (32 rows) of one camera view -- 10 units per scene, one CTA per unit,
+ *    CTAs striding over units.  Each unit traces from a single origin, so the
+ *    ray-independent sphere terms (o - c, |o - c|^2, r^2) and the dome's
+ *    constant term are formed once per CTA in shared memory and read as warp
+ *    broadcasts (two 128-bit and one 64-bit load per sphere).
+ *  - Sphere culling per unit: a sphere whose surface lies farther than the
+ *    sky distance can never beat it, and a unit's rays lie in a cone (axis
+ *    and half-angle per unit, from the ray tables).  A sphere that every ray
+ *    of the cone misses by a margin -- the exact discriminant at most
+ *    -1e-12 * max(1, L)^2 against a rounding error below 1e-14 * L^2, or the
+ *    whole sphere behind the origin by more than 0.1 m -- would return "no
+ *    hit" for every ray.  Either way the sphere is left out of that unit's
+ *    list; the remaining spheres keep their order.  Only unit attitudes
+ *    (|q|^2 within 1e-9 of 1) with finite geometry are culled; anything else
+ *    keeps every sphere.  Likewise the arena dome is skipped for a unit whose
+ *    origin is so far inside it that every dome hit lies beyond the sky.
  *  - Body-frame ray directions do not depend on the scene: they are built on
  *    the host with the C library the simulator uses (sensor_rays.c) and read
  *    from global memory (SoA, coalesced); the kernel only rotates them.
@@ -26,11 +37,13 @@
  *    expression order and no multiply-add contraction (this file is built
  *    with -fmad=false); double division and square root are correctly
  *    rounded, so ranges equal the simulator's bit for bit.  The only
- *    transcendental per ray is the camera's exp(-d/80).
+ *    transcendental per ray is the camera's exp(-d/80), evaluated once per
+ *    unit for sky pixels (whose distance is the unit's constant sky distance).
  *  - Camera bytes are written four pixels per 32-bit store (a warp covers 128
  *    contiguous bytes); the optional raw capture writes each pixel 3 x 3.
- *  The work is FP64-pipe bound (no tensor-core or HBM bound applies): about
- *  35 double operations to rotate a ray plus about 8 per sphere tested.
+ *  The work is FP64-pipe and issue bound (no tensor-core or HBM bound
+ *  applies): about 35 double operations to rotate a ray plus about 8 per
+ *  sphere tested.
  */
 #include <cuda_runtime.h>
 
@@ -42,22 +55,38 @@
 #include "tb_sensor_rays.h"
 #include "turbinator/sim/cuda_sensors.h"
 
+#ifndef TB_SENSOR_THREADS
+#define TB_SENSOR_THREADS 256
+#endif
+#ifndef TB_SENSOR_MIN_BLOCKS
+#define TB_SENSOR_MIN_BLOCKS 4
+#endif
+#ifndef TB_SENSOR_CULL
+#define TB_SENSOR_CULL 1
+#endif
+
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = TB_SENSOR_THREADS;
+constexpr int kWarps = kThreads / 32;
 constexpr int kUnitRays = 2048;
 constexpr int kUnitsPerScene = 10; /* 2 LiDAR heads + 4 views x 2 halves */
 constexpr int kMaxSpheres = TB_SENSOR_MAX_OBSTACLES + 1 + TB_SENSOR_MAX_BALLS;
+constexpr int kSphereWarps = (kMaxSpheres + 31) / 32;
 constexpr int kLidarBins = TB_SENSOR_LIDAR_BINS;
 constexpr int kCameraPixels = TB_SENSOR_CAMERA_PIXELS;
 constexpr unsigned long long kGolden = 0x9e3779b97f4a7c15ull;
 
 static_assert(sizeof(tb_sensor_scene) == 2432, "scene record layout");
+static_assert(kThreads >= 32 * kSphereWarps && kUnitRays % (4 * kThreads) == 0, "unit split");
 
 /* Body-frame directions, structure of arrays. */
 __device__ double g_lidar_x[kLidarBins], g_lidar_y[kLidarBins], g_lidar_z[kLidarBins];
 __device__ unsigned int g_lidar_blocked[kLidarBins / 32];
 __device__ double g_camera_x[kCameraPixels], g_camera_y[kCameraPixels], g_camera_z[kCameraPixels];
+/* Per unit kind: body-frame cone axis (unit) and cos, sin of its half-angle
+ * widened by 1e-6 rad. */
+__device__ double g_cone[kUnitsPerScene][5];
 
 struct Vec {
     double x, y, z;
@@ -78,26 +107,33 @@ __device__ __forceinline__ bool is_arena(int s) {
 
 /* One unit's scene, prepared for tracing from one origin. */
 struct UnitScene {
-    double ocx[kMaxSpheres], ocy[kMaxSpheres], ocz[kMaxSpheres]; /* origin - centre */
-    double occ[kMaxSpheres];                                     /* |origin - centre|^2 */
-    double rr[kMaxSpheres];                                      /* radius^2 */
+    double2 oc_xy[kMaxSpheres]; /* origin - centre, x y */
+    double2 oc_zq[kMaxSpheres]; /* origin - centre z, |origin - centre|^2 */
+    double rr[kMaxSpheres];     /* radius^2 */
     double q[4];
     double origin[3];
+    double axis[3];   /* the unit's cone axis in the world frame */
     double best0;     /* trace()'s starting distance (also the sky distance) */
+    double sky_fog;   /* shade()'s distance factor at best0 */
     double max_range; /* LiDAR clamp */
     double dome_cc;   /* o.x^2 + o.y^2 - dome^2 */
     unsigned long long seed;
-    int obstacles, opponent, balls; /* sphere counts, in trace order */
-    int shelf;                      /* scenario 10's raised ground at z = 9, x >= 20 */
-    int skip;                       /* this unit renders nothing */
-    int valid[kThreads / 32];
+    int n_obstacles, n_balls, arena; /* scene counts (clamped) */
+    int dome;                        /* the dome can be hit before the sky distance */
+    int cull;                        /* the attitude is a rotation: culling allowed */
+    int kept_obstacles, kept_opponent, kept_total; /* the unit's list, in trace order */
+    int shelf;                       /* scenario 10's raised ground at z = 9, x >= 20 */
+    int skip;                        /* this unit renders nothing */
+    unsigned int keep_mask[kSphereWarps], obst_mask[kSphereWarps], opp_mask[kSphereWarps];
+    int valid[kWarps];
 };
 
 /* sphere_hit (sensors.c:4-10) with the ray-independent terms precomputed in
  * the same rounding: b = oc.d, disc = (b*b - oc.oc) + r*r. */
 __device__ __forceinline__ double sphere_hit(const UnitScene &s, int i, Vec d) {
-    const double b = s.ocx[i] * d.x + s.ocy[i] * d.y + s.ocz[i] * d.z;
-    const double disc = b * b - s.occ[i] + s.rr[i];
+    const double2 xy = s.oc_xy[i], zq = s.oc_zq[i];
+    const double b = xy.x * d.x + xy.y * d.y + zq.x * d.z;
+    const double disc = b * b - zq.y + s.rr[i];
     if (disc < 0) return INFINITY;
     const double root = sqrt(disc);
     double t = -b - root;
@@ -127,32 +163,35 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
         }
     }
     int i = 0;
-    for (; i < s.obstacles; ++i) {
+    for (; i < s.kept_obstacles; ++i) {
         const double t = sphere_hit(s, i, d);
         if (t < best) {
             best = t;
             kind = 1;
         }
     }
-    if (s.opponent) {
-        const double t = sphere_hit(s, i, d);
-        if (t < best) {
-            best = t;
-            kind = 2;
+    if (s.arena) {
+        if (s.kept_opponent) {
+            const double t = sphere_hit(s, i, d);
+            if (t < best) {
+                best = t;
+                kind = 2;
+            }
+            ++i;
         }
-        ++i;
-        const double a = d.x * d.x + d.y * d.y, b = 2 * (ox * d.x + oy * d.y);
-        const double disc = b * b - 4 * a * s.dome_cc;
-        if (a > 1e-9 && disc >= 0) {
-            const double td = (-b + sqrt(disc)) / (2 * a);
-            if (td > 0.05 && td < best) {
-                best = td;
-                kind = 3;
+        if (s.dome) {
+            const double a = d.x * d.x + d.y * d.y, b = 2 * (ox * d.x + oy * d.y);
+            const double disc = b * b - 4 * a * s.dome_cc;
+            if (a > 1e-9 && disc >= 0) {
+                const double td = (-b + sqrt(disc)) / (2 * a);
+                if (td > 0.05 && td < best) {
+                    best = td;
+                    kind = 3;
+                }
             }
         }
     }
-    const int end = i + s.balls;
-    for (; i < end; ++i) {
+    for (; i < s.kept_total; ++i) {
         const double t = sphere_hit(s, i, d);
         if (t < best) {
             best = t;
@@ -162,15 +201,18 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
     return best;
 }
 
-/* shade (sensors.c:59-68). */
-__device__ __forceinline__ uint32_t shade(double distance, int kind, double dz) {
+/* shade()'s distance factor, sensors.c:66. */
+__device__ __forceinline__ double fog(double distance) { return 0.75 + 0.25 * exp(-distance / 80); }
+
+/* shade (sensors.c:59-68); the sky's factor comes precomputed. */
+__device__ __forceinline__ uint32_t shade(const UnitScene &s, double distance, int kind, double dz) {
     double luma = 0.22 + 0.15 * fmax(-1.0, fmin(1.0, dz));
     if (kind == 0) luma = 0.28 + 0.17 * fmax(0.0, fmin(1.0, -dz));
     if (kind == 1) luma = 0.65;
     if (kind == 2) luma = 0.90;
     if (kind == 3) luma = 0.46;
     if (kind == 4) luma = 1.0;
-    luma *= 0.75 + 0.25 * exp(-distance / 80);
+    luma *= kind < 0 ? s.sky_fog : fog(distance);
     return static_cast<uint32_t>(fmax(0.0, fmin(255.0, round(luma * 255))));
 }
 
@@ -178,6 +220,29 @@ __device__ __forceinline__ unsigned long long splitmix(unsigned long long z) {
     z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
     z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
     return z ^ (z >> 31);
+}
+
+/* True when no ray of the unit's cone can take the sphere (centre c, radius
+ * r) as its nearest hit from origin o: the sphere's surface lies beyond the
+ * sky distance (every hit t >= L - r), or every ray provably returns "no
+ * hit" -- the sphere lies wholly behind the origin, or each ray's closest
+ * approach to the centre exceeds the radius by 1e-6 * max(1, L).  NaN and
+ * infinite inputs give false. */
+__device__ __forceinline__ bool cone_misses(const UnitScene &s, const double *cone, double cx, double cy, double cz,
+                                            double r) {
+    const double wx = cx - s.origin[0], wy = cy - s.origin[1], wz = cz - s.origin[2];
+    const double l = sqrt(wx * wx + wy * wy + wz * wz);
+    const double ra = fabs(r);
+    if (!(l < 1e7) || !(l > ra + 0.1)) return false; /* also rejects NaN */
+    if (l - ra > s.best0 * (1 + 1e-9) + 1e-9) return true;
+    const double cosc = fmin(1.0, fmax(-1.0, (wx * s.axis[0] + wy * s.axis[1] + wz * s.axis[2]) / l));
+    const double sinc = sqrt(fmax(0.0, 1.0 - cosc * cosc));
+    const double cos_a = cone[3], sin_a = cone[4];
+    /* the smallest angle between a ray of the cone and the centre direction */
+    const double sin_min = sinc * cos_a - cosc * sin_a;
+    const double cos_min = cosc * cos_a + sinc * sin_a;
+    if (cos_min < -1e-9 && sin_min > 0) return true; /* every ray points away */
+    return sin_min > 0 && l * sin_min > ra + 1e-6 * fmax(1.0, l);
 }
 
 /* Loads the unit's scene and forms its per-origin terms (all threads). */
@@ -189,78 +254,125 @@ __device__ void prepare_unit(UnitScene &s, const tb_sensor_scene *__restrict__ s
         const bool want = part < 2 ? (lidar_out && (sensors & TB_SENSOR_LIDAR))
                                    : (camera_out && (sensors & TB_SENSOR_CAMERA));
         s.skip = !want;
-        const int scenario = scene->scenario;
-        const bool bwb = is_bwb(scenario), arena = is_arena(scenario);
-        const double qw = scene->attitude[0], qx = scene->attitude[1], qy = scene->attitude[2],
-                     qz = scene->attitude[3];
-        s.q[0] = qw;
-        s.q[1] = qx;
-        s.q[2] = qy;
-        s.q[3] = qz;
-        /* Sensor mounts: LiDAR heads sensors.c:32, cameras :72. */
-        Vec mount;
-        if (part < 2) {
-            mount = Vec{0.4, 0.4, part ? -0.4 : 0.4};
-        } else {
-            const int view = (part - 2) >> 1;
-            mount = view < 2 ? Vec{0.42, 0.42, view == 0 ? 0.13 : 0.08} : Vec{0, 0, view == 2 ? -0.5 : 0.5};
+        if (want) {
+            const int scenario = scene->scenario;
+            const bool bwb = is_bwb(scenario), arena = is_arena(scenario);
+            const double qw = scene->attitude[0], qx = scene->attitude[1], qy = scene->attitude[2],
+                         qz = scene->attitude[3];
+            s.q[0] = qw;
+            s.q[1] = qx;
+            s.q[2] = qy;
+            s.q[3] = qz;
+            /* Sensor mounts: LiDAR heads sensors.c:32, cameras :72. */
+            Vec mount;
+            if (part < 2) {
+                mount = Vec{0.4, 0.4, part ? -0.4 : 0.4};
+            } else {
+                const int view = (part - 2) >> 1;
+                mount = view < 2 ? Vec{0.42, 0.42, view == 0 ? 0.13 : 0.08} : Vec{0, 0, view == 2 ? -0.5 : 0.5};
+            }
+            const Vec r = rotate(qw, qx, qy, qz, mount);
+            const double ox = scene->position[0] + r.x, oy = scene->position[1] + r.y,
+                         oz = scene->position[2] + r.z;
+            s.origin[0] = ox;
+            s.origin[1] = oy;
+            s.origin[2] = oz;
+            const Vec axis = rotate(qw, qx, qy, qz, Vec{g_cone[part][0], g_cone[part][1], g_cone[part][2]});
+            s.axis[0] = axis.x;
+            s.axis[1] = axis.y;
+            s.axis[2] = axis.z;
+            const double norm2 = qw * qw + qx * qx + qy * qy + qz * qz;
+            s.cull = TB_SENSOR_CULL && fabs(norm2 - 1.0) < 1e-9;
+            const double lidar_max = scene->lidar_max;
+            s.best0 = bwb ? fmax(lidar_max, 120.0) : lidar_max;
+            s.sky_fog = fog(s.best0);
+            s.max_range = bwb ? fmax(120.0, lidar_max) : lidar_max;
+            const double dome = bwb ? 300.0 : scene->dome_radius;
+            s.dome_cc = ox * ox + oy * oy - dome * dome;
+            /* Inside the cylinder at horizontal radius rho, a dome hit needs a
+             * horizontal run of at least dome - rho, so t >= dome - rho. */
+            const double rho = sqrt(ox * ox + oy * oy);
+            s.dome = !(TB_SENSOR_CULL && dome - rho > s.best0 * (1 + 1e-9) + 1e-9);
+            s.shelf = scenario == 10;
+            s.arena = arena;
+            s.n_obstacles = min(max(scene->obstacle_count, 0), TB_SENSOR_MAX_OBSTACLES);
+            s.n_balls = min(max(scene->ball_count, 0), TB_SENSOR_MAX_BALLS);
+            /* sensors.c:30: rng ^ step_index * golden ^ player * 257 */
+            s.seed = scene->rng ^
+                     (static_cast<unsigned long long>(static_cast<long long>(scene->step_index)) * kGolden) ^
+                     static_cast<unsigned long long>(static_cast<long long>(scene->player) * 257);
         }
-        const Vec r = rotate(qw, qx, qy, qz, mount);
-        const double ox = scene->position[0] + r.x, oy = scene->position[1] + r.y, oz = scene->position[2] + r.z;
-        s.origin[0] = ox;
-        s.origin[1] = oy;
-        s.origin[2] = oz;
-        const double lidar_max = scene->lidar_max;
-        s.best0 = bwb ? fmax(lidar_max, 120.0) : lidar_max;
-        s.max_range = bwb ? fmax(120.0, lidar_max) : lidar_max;
-        const double dome = bwb ? 300.0 : scene->dome_radius;
-        s.dome_cc = ox * ox + oy * oy - dome * dome;
-        s.shelf = scenario == 10;
-        s.obstacles = min(max(scene->obstacle_count, 0), TB_SENSOR_MAX_OBSTACLES);
-        s.opponent = arena;
-        s.balls = min(max(scene->ball_count, 0), TB_SENSOR_MAX_BALLS);
-        /* sensors.c:30: rng ^ step_index * golden ^ player * 257 */
-        s.seed = scene->rng ^ (static_cast<unsigned long long>(static_cast<long long>(scene->step_index)) * kGolden) ^
-                 static_cast<unsigned long long>(static_cast<long long>(scene->player) * 257);
     }
     __syncthreads();
     if (s.skip) return;
-    const int n = s.obstacles + s.opponent + s.balls;
-    if (t < n) {
-        double cx, cy, cz, radius;
-        if (t < s.obstacles) {
-            cx = scene->obstacles[t][0];
-            cy = scene->obstacles[t][1];
-            cz = scene->obstacles[t][2];
-            radius = scene->obstacles[t][3];
-        } else if (s.opponent && t == s.obstacles) {
-            cx = scene->opponent[0];
-            cy = scene->opponent[1];
-            cz = scene->opponent[2];
-            radius = is_bwb(scene->scenario) ? 0.75 : 0.45;
-        } else {
-            const int j = t - s.obstacles - s.opponent;
-            cx = scene->balls[j][0];
-            cy = scene->balls[j][1];
-            cz = scene->balls[j][2];
-            radius = 0.25;
+    /* Spheres in trace order: obstacles, the arena opponent, balls. */
+    const int n = s.n_obstacles + s.arena + s.n_balls;
+    double ocx = 0, ocy = 0, ocz = 0, occ = 0, rr = 0;
+    bool keep = false;
+    if (t < 32 * kSphereWarps) {
+        if (t < n) {
+            double cx, cy, cz, radius;
+            if (t < s.n_obstacles) {
+                cx = scene->obstacles[t][0];
+                cy = scene->obstacles[t][1];
+                cz = scene->obstacles[t][2];
+                radius = scene->obstacles[t][3];
+            } else if (s.arena && t == s.n_obstacles) {
+                cx = scene->opponent[0];
+                cy = scene->opponent[1];
+                cz = scene->opponent[2];
+                radius = is_bwb(scene->scenario) ? 0.75 : 0.45;
+            } else {
+                const int j = t - s.n_obstacles - s.arena;
+                cx = scene->balls[j][0];
+                cy = scene->balls[j][1];
+                cz = scene->balls[j][2];
+                radius = 0.25;
+            }
+            ocx = s.origin[0] - cx;
+            ocy = s.origin[1] - cy;
+            ocz = s.origin[2] - cz;
+            occ = ocx * ocx + ocy * ocy + ocz * ocz;
+            rr = radius * radius;
+            keep = !(s.cull && cone_misses(s, g_cone[part], cx, cy, cz, radius));
         }
-        const double ocx = s.origin[0] - cx, ocy = s.origin[1] - cy, ocz = s.origin[2] - cz;
-        s.ocx[t] = ocx;
-        s.ocy[t] = ocy;
-        s.ocz[t] = ocz;
-        s.occ[t] = ocx * ocx + ocy * ocy + ocz * ocz;
-        s.rr[t] = radius * radius;
+        const unsigned int m = __ballot_sync(0xffffffffu, keep);
+        const unsigned int obst = __ballot_sync(0xffffffffu, keep && t < s.n_obstacles);
+        const unsigned int opp = __ballot_sync(0xffffffffu, keep && s.arena && t == s.n_obstacles);
+        if ((t & 31) == 0) {
+            s.keep_mask[t >> 5] = m;
+            s.obst_mask[t >> 5] = obst;
+            s.opp_mask[t >> 5] = opp;
+        }
+    }
+    __syncthreads();
+    if (t < 32 * kSphereWarps) {
+        const int w = t >> 5;
+        int pos = __popc(s.keep_mask[w] & ((1u << (t & 31)) - 1u));
+        for (int k = 0; k < w; ++k) pos += __popc(s.keep_mask[k]);
+        if (keep) {
+            s.oc_xy[pos] = make_double2(ocx, ocy);
+            s.oc_zq[pos] = make_double2(ocz, occ);
+            s.rr[pos] = rr;
+        }
+        if (t == 0) {
+            int total = 0, kept_obst = 0, kept_opp = 0;
+            for (int k = 0; k < kSphereWarps; ++k) {
+                total += __popc(s.keep_mask[k]);
+                kept_obst += __popc(s.obst_mask[k]);
+                kept_opp += __popc(s.opp_mask[k]);
+            }
+            s.kept_total = total;
+            s.kept_obstacles = kept_obst;
+            s.kept_opponent = kept_opp;
+        }
     }
 }
 
-__global__ void __launch_bounds__(kThreads) sensors_kernel(const tb_sensor_scene *__restrict__ scenes,
-                                                           unsigned long long units, float *__restrict__ lidar,
-                                                           unsigned long long lidar_stride,
-                                                           float *__restrict__ lidar_valid,
-                                                           unsigned long long valid_stride,
-                                                           unsigned char *__restrict__ cameras,
-                                                           unsigned char *__restrict__ raw) {
+__global__ void __launch_bounds__(kThreads, TB_SENSOR_MIN_BLOCKS)
+    sensors_kernel(const tb_sensor_scene *__restrict__ scenes, unsigned long long units, float *__restrict__ lidar,
+                   unsigned long long lidar_stride, float *__restrict__ lidar_valid, unsigned long long valid_stride,
+                   unsigned char *__restrict__ cameras, unsigned char *__restrict__ raw) {
     __shared__ UnitScene s;
     const int t = threadIdx.x;
     for (unsigned long long unit = blockIdx.x; unit < units; unit += gridDim.x) {
@@ -299,7 +411,7 @@ __global__ void __launch_bounds__(kThreads) sensors_kernel(const tb_sensor_scene
                 __syncthreads();
                 if (t == 0) {
                     int total = 0;
-                    for (int w = 0; w < kThreads / 32; ++w) total += s.valid[w];
+                    for (int w = 0; w < kWarps; ++w) total += s.valid[w];
                     lidar_valid[scene_index * valid_stride + part] = static_cast<float>(total) / 2048;
                 }
             }
@@ -311,13 +423,13 @@ __global__ void __launch_bounds__(kThreads) sensors_kernel(const tb_sensor_scene
                 const int local = half * kUnitRays + k * 4 * kThreads + 4 * t; /* pixel in the view */
                 const int pixel = view * 4096 + local;
                 uint32_t word = 0;
-#pragma unroll
+#pragma unroll 1
                 for (int j = 0; j < 4; ++j) {
                     const Vec dir = rotate(qw, qx, qy, qz,
                                            Vec{g_camera_x[pixel + j], g_camera_y[pixel + j], g_camera_z[pixel + j]});
                     int kind;
                     const double d = trace(s, dir, kind);
-                    word |= shade(d, kind, dir.z) << (8 * j);
+                    word |= shade(s, d, kind, dir.z) << (8 * j);
                 }
                 if (cameras)
                     *reinterpret_cast<uint32_t *>(cameras + scene_index * kCameraPixels + pixel) = word;
@@ -349,7 +461,38 @@ bool g_tables_ready[kMaxDevices];
 int g_grid_cap[kMaxDevices];
 std::mutex g_tables_mutex;
 
-/* Uploads the body-frame ray tables to the current device (once). */
+/* Cone of unit `part` over body-frame rays dirs[first .. first+count) (rays
+ * with skip[i] set are never traced): unit axis, then cos and sin of the
+ * largest angle to any ray widened by 1e-6 rad. */
+void unit_cone(const double *x, const double *y, const double *z, int first, int count, const unsigned char *skip,
+               double *cone) {
+    double ax = 0, ay = 0, az = 0;
+    for (int i = first; i < first + count; ++i)
+        if (!skip || !skip[i]) {
+            ax += x[i];
+            ay += y[i];
+            az += z[i];
+        }
+    const double n = sqrt(ax * ax + ay * ay + az * az);
+    ax /= n;
+    ay /= n;
+    az /= n;
+    double widest = 0;
+    for (int i = first; i < first + count; ++i) {
+        if (skip && skip[i]) continue;
+        const double len = sqrt(x[i] * x[i] + y[i] * y[i] + z[i] * z[i]);
+        const double c = fmin(1.0, fmax(-1.0, (x[i] * ax + y[i] * ay + z[i] * az) / len));
+        widest = fmax(widest, acos(c));
+    }
+    widest += 1e-6;
+    cone[0] = ax;
+    cone[1] = ay;
+    cone[2] = az;
+    cone[3] = cos(widest);
+    cone[4] = sin(widest);
+}
+
+/* Uploads the body-frame ray tables and unit cones to the current device (once). */
 bool ensure_tables(int dev) {
     std::lock_guard<std::mutex> lock(g_tables_mutex);
     if (g_tables_ready[dev]) return true;
@@ -359,6 +502,7 @@ bool ensure_tables(int dev) {
     static double lx[kLidarBins], ly[kLidarBins], lz[kLidarBins];
     static double cx[kCameraPixels], cy[kCameraPixels], cz[kCameraPixels];
     static unsigned int mask[kLidarBins / 32];
+    static double cones[kUnitsPerScene][5];
     if (!built) {
         tb_sensor_lidar_rays(lidar_dirs, blocked);
         tb_sensor_camera_rays(camera_dirs);
@@ -373,6 +517,9 @@ bool ensure_tables(int dev) {
             cy[i] = camera_dirs[3 * i + 1];
             cz[i] = camera_dirs[3 * i + 2];
         }
+        for (int h = 0; h < 2; ++h) unit_cone(lx, ly, lz, h * kUnitRays, kUnitRays, blocked, cones[h]);
+        for (int p = 2; p < kUnitsPerScene; ++p)
+            unit_cone(cx, cy, cz, ((p - 2) >> 1) * 4096 + ((p - 2) & 1) * kUnitRays, kUnitRays, nullptr, cones[p]);
         built = true;
     }
     int sms = 0, blocks = 0;
@@ -383,6 +530,7 @@ bool ensure_tables(int dev) {
         cudaMemcpyToSymbol(g_camera_x, cx, sizeof cx) != cudaSuccess ||
         cudaMemcpyToSymbol(g_camera_y, cy, sizeof cy) != cudaSuccess ||
         cudaMemcpyToSymbol(g_camera_z, cz, sizeof cz) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_cone, cones, sizeof cones) != cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, sensors_kernel, kThreads, 0) != cudaSuccess)
         return false;
