@@ -223,6 +223,22 @@ def test_multi_device_handle_shards_and_gathers(devices, n):
     check_features(out, oracle.features(obs, mission, cams), f"multi {devices}")
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_multi_device_handle_on_distinct_gpus():
+    """The sample-sharded handle over every visible GPU: each device holds its
+    own staging and runs its slice concurrently; rows come back in order."""
+    devices = list(range(torch.cuda.device_count()))
+    n = 9001
+    obs, mission, cams, _ = tb.generate(33, 0, n)
+    expected = oracle.features(obs, mission, cams)
+    out = np.zeros((n, 142), np.float32)
+    with tb.FeatureBatch(devices, n) as fb:
+        for count in (n, 5, len(devices) - 1 or 1):
+            out[:] = 0
+            assert fb.extract(obs, mission, cams, count, out) == 1, fb.error()
+            check_features(out[:count], expected[:count], f"distinct GPUs {devices} count={count}")
+
+
 def test_multi_device_handle_rejects_bad_devices():
     assert tb.tb_cuda_feature_batch_create_multi([0, 10_000], 16) is None
     assert tb.tb_cuda_feature_batch_create_multi([], 16) is None

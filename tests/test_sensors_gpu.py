@@ -160,6 +160,25 @@ def test_non_default_stream():
     assert_same(got, (want[0], want[1], want[2], None), "stream")
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_every_visible_gpu_renders_the_same():
+    """The ray tables are uploaded per device on first use; every GPU renders
+    the golden scenes exactly."""
+    g = np.load(GOLDEN)
+    scenes = g["scenes"].view(SCENE_DTYPE).reshape(-1)
+    n = len(scenes)
+    for dev in range(torch.cuda.device_count()):
+        with torch.cuda.device(dev):
+            d = torch.from_numpy(scenes.view(np.uint8).reshape(-1).copy()).to(f"cuda:{dev}")
+            lidar = torch.full((n, 4096), float("nan"), device=f"cuda:{dev}")
+            valid = torch.full((n, 2), float("nan"), device=f"cuda:{dev}")
+            cams = torch.zeros((n, 16384), dtype=torch.uint8, device=f"cuda:{dev}")
+            assert tb_cuda_render_sensors_device(d, n, lidar, 4096, valid, 2, cams) == 1
+            torch.cuda.synchronize(dev)
+            assert_same((lidar.cpu().numpy(), valid.cpu().numpy(), cams.cpu().numpy(), None),
+                        (g["lidar"], g["valid"], g["cameras"], None), f"cuda:{dev}")
+
+
 @needs_reference
 def test_full_batch_sampled_and_deterministic():
     n = 65536
