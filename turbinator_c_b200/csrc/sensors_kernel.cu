@@ -15,7 +15,10 @@
  *    CTAs striding over units.  Each unit traces from a single origin, so the
  *    ray-independent sphere terms (o - c, |o - c|^2, r^2) and the dome's
  *    constant term are formed once per CTA in shared memory and read as warp
- *    broadcasts (two 128-bit and one 64-bit load per sphere).
+ *    broadcasts (two 128-bit and one 64-bit load per sphere).  Two
+ *    shared-memory slots alternate over a CTA's units, so a unit costs two CTA
+ *    barriers (both while its sphere list is formed); the LiDAR valid count is
+ *    summed with shared-memory atomics and written by the last warp.
  *  - Sphere culling per unit: a sphere whose surface lies farther than the
  *    sky distance can never beat it, and a unit's rays lie in a cone (axis
  *    and half-angle per unit, from the ray tables).  A sphere that every ray
@@ -105,11 +108,8 @@ __device__ __forceinline__ bool is_arena(int s) {
     return s == 3 || s == 14 || s == 15 || s == 16 || s == 18 || s == 22 || s == 24 || s == 27;
 }
 
-/* One unit's scene, prepared for tracing from one origin. */
-struct UnitScene {
-    double2 oc_xy[kMaxSpheres]; /* origin - centre, x y */
-    double2 oc_zq[kMaxSpheres]; /* origin - centre z, |origin - centre|^2 */
-    double rr[kMaxSpheres];     /* radius^2 */
+/* A unit's per-origin scalars. */
+struct UnitHead {
     double q[4];
     double origin[3];
     double axis[3];   /* the unit's cone axis in the world frame */
@@ -121,11 +121,18 @@ struct UnitScene {
     int n_obstacles, n_balls, arena; /* scene counts (clamped) */
     int dome;                        /* the dome can be hit before the sky distance */
     int cull;                        /* the attitude is a rotation: culling allowed */
-    int kept_obstacles, kept_opponent, kept_total; /* the unit's list, in trace order */
     int shelf;                       /* scenario 10's raised ground at z = 9, x >= 20 */
-    int skip;                        /* this unit renders nothing */
+};
+
+/* One unit's scene, prepared for tracing from one origin. */
+struct UnitScene {
+    double2 oc_xy[kMaxSpheres]; /* origin - centre, x y */
+    double2 oc_zq[kMaxSpheres]; /* origin - centre z, |origin - centre|^2 */
+    double rr[kMaxSpheres];     /* radius^2 */
+    UnitHead h;
+    int kept_obstacles, kept_opponent, kept_total; /* the unit's list, in trace order */
     unsigned int keep_mask[kSphereWarps], obst_mask[kSphereWarps], opp_mask[kSphereWarps];
-    int valid[kWarps];
+    int valid_count, warps_done; /* LiDAR valid rays of the unit, warps finished */
 };
 
 /* sphere_hit (sensors.c:4-10) with the ray-independent terms precomputed in
@@ -145,16 +152,16 @@ __device__ __forceinline__ double sphere_hit(const UnitScene &s, int i, Vec d) {
  * simulator's test order (ground, shelf, obstacles, opponent, dome, balls);
  * kind -1 sky, 0 ground, 1 obstacle, 2 opponent, 3 dome, 4 ball. */
 __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
-    double best = s.best0;
+    double best = s.h.best0;
     kind = -1;
-    const double ox = s.origin[0], oy = s.origin[1], oz = s.origin[2];
+    const double ox = s.h.origin[0], oy = s.h.origin[1], oz = s.h.origin[2];
     if (d.z < -1e-5) {
         const double t = (0 - oz) / d.z;
         if (t > 0.05 && t < best) {
             best = t;
             kind = 0;
         }
-        if (s.shelf) {
+        if (s.h.shelf) {
             const double t2 = (9 - oz) / d.z;
             if (t2 > 0.05 && t2 < best && ox + t2 * d.x >= 20) {
                 best = t2;
@@ -170,7 +177,7 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
             kind = 1;
         }
     }
-    if (s.arena) {
+    if (s.h.arena) {
         if (s.kept_opponent) {
             const double t = sphere_hit(s, i, d);
             if (t < best) {
@@ -179,9 +186,9 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
             }
             ++i;
         }
-        if (s.dome) {
+        if (s.h.dome) {
             const double a = d.x * d.x + d.y * d.y, b = 2 * (ox * d.x + oy * d.y);
-            const double disc = b * b - 4 * a * s.dome_cc;
+            const double disc = b * b - 4 * a * s.h.dome_cc;
             if (a > 1e-9 && disc >= 0) {
                 const double td = (-b + sqrt(disc)) / (2 * a);
                 if (td > 0.05 && td < best) {
@@ -212,7 +219,7 @@ __device__ __forceinline__ uint32_t shade(const UnitScene &s, double distance, i
     if (kind == 2) luma = 0.90;
     if (kind == 3) luma = 0.46;
     if (kind == 4) luma = 1.0;
-    luma *= kind < 0 ? s.sky_fog : fog(distance);
+    luma *= kind < 0 ? s.h.sky_fog : fog(distance);
     return static_cast<uint32_t>(fmax(0.0, fmin(255.0, round(luma * 255))));
 }
 
@@ -228,14 +235,14 @@ __device__ __forceinline__ unsigned long long splitmix(unsigned long long z) {
  * hit" -- the sphere lies wholly behind the origin, or each ray's closest
  * approach to the centre exceeds the radius by 1e-6 * max(1, L).  NaN and
  * infinite inputs give false. */
-__device__ __forceinline__ bool cone_misses(const UnitScene &s, const double *cone, double cx, double cy, double cz,
+__device__ __forceinline__ bool cone_misses(const UnitHead &h, const double *cone, double cx, double cy, double cz,
                                             double r) {
-    const double wx = cx - s.origin[0], wy = cy - s.origin[1], wz = cz - s.origin[2];
+    const double wx = cx - h.origin[0], wy = cy - h.origin[1], wz = cz - h.origin[2];
     const double l = sqrt(wx * wx + wy * wy + wz * wz);
     const double ra = fabs(r);
     if (!(l < 1e7) || !(l > ra + 0.1)) return false; /* also rejects NaN */
-    if (l - ra > s.best0 * (1 + 1e-9) + 1e-9) return true;
-    const double cosc = fmin(1.0, fmax(-1.0, (wx * s.axis[0] + wy * s.axis[1] + wz * s.axis[2]) / l));
+    if (l - ra > h.best0 * (1 + 1e-9) + 1e-9) return true;
+    const double cosc = fmin(1.0, fmax(-1.0, (wx * h.axis[0] + wy * h.axis[1] + wz * h.axis[2]) / l));
     const double sinc = sqrt(fmax(0.0, 1.0 - cosc * cosc));
     const double cos_a = cone[3], sin_a = cone[4];
     /* the smallest angle between a ray of the cone and the centre direction */
@@ -245,100 +252,104 @@ __device__ __forceinline__ bool cone_misses(const UnitScene &s, const double *co
     return sin_min > 0 && l * sin_min > ra + 1e-6 * fmax(1.0, l);
 }
 
-/* Loads the unit's scene and forms its per-origin terms (all threads). */
-__device__ void prepare_unit(UnitScene &s, const tb_sensor_scene *__restrict__ scene, int part, bool lidar_out,
-                             bool camera_out) {
-    const int t = threadIdx.x;
-    if (t == 0) {
-        const int sensors = scene->sensors;
-        const bool want = part < 2 ? (lidar_out && (sensors & TB_SENSOR_LIDAR))
-                                   : (camera_out && (sensors & TB_SENSOR_CAMERA));
-        s.skip = !want;
-        if (want) {
-            const int scenario = scene->scenario;
-            const bool bwb = is_bwb(scenario), arena = is_arena(scenario);
-            const double qw = scene->attitude[0], qx = scene->attitude[1], qy = scene->attitude[2],
-                         qz = scene->attitude[3];
-            s.q[0] = qw;
-            s.q[1] = qx;
-            s.q[2] = qy;
-            s.q[3] = qz;
-            /* Sensor mounts: LiDAR heads sensors.c:32, cameras :72. */
-            Vec mount;
-            if (part < 2) {
-                mount = Vec{0.4, 0.4, part ? -0.4 : 0.4};
-            } else {
-                const int view = (part - 2) >> 1;
-                mount = view < 2 ? Vec{0.42, 0.42, view == 0 ? 0.13 : 0.08} : Vec{0, 0, view == 2 ? -0.5 : 0.5};
-            }
-            const Vec r = rotate(qw, qx, qy, qz, mount);
-            const double ox = scene->position[0] + r.x, oy = scene->position[1] + r.y,
-                         oz = scene->position[2] + r.z;
-            s.origin[0] = ox;
-            s.origin[1] = oy;
-            s.origin[2] = oz;
-            const Vec axis = rotate(qw, qx, qy, qz, Vec{g_cone[part][0], g_cone[part][1], g_cone[part][2]});
-            s.axis[0] = axis.x;
-            s.axis[1] = axis.y;
-            s.axis[2] = axis.z;
-            const double norm2 = qw * qw + qx * qx + qy * qy + qz * qz;
-            s.cull = TB_SENSOR_CULL && fabs(norm2 - 1.0) < 1e-9;
-            const double lidar_max = scene->lidar_max;
-            s.best0 = bwb ? fmax(lidar_max, 120.0) : lidar_max;
-            s.sky_fog = fog(s.best0);
-            s.max_range = bwb ? fmax(120.0, lidar_max) : lidar_max;
-            const double dome = bwb ? 300.0 : scene->dome_radius;
-            s.dome_cc = ox * ox + oy * oy - dome * dome;
-            /* Inside the cylinder at horizontal radius rho, a dome hit needs a
-             * horizontal run of at least dome - rho, so t >= dome - rho. */
-            const double rho = sqrt(ox * ox + oy * oy);
-            s.dome = !(TB_SENSOR_CULL && dome - rho > s.best0 * (1 + 1e-9) + 1e-9);
-            s.shelf = scenario == 10;
-            s.arena = arena;
-            s.n_obstacles = min(max(scene->obstacle_count, 0), TB_SENSOR_MAX_OBSTACLES);
-            s.n_balls = min(max(scene->ball_count, 0), TB_SENSOR_MAX_BALLS);
-            /* sensors.c:30: rng ^ step_index * golden ^ player * 257 */
-            s.seed = scene->rng ^
-                     (static_cast<unsigned long long>(static_cast<long long>(scene->step_index)) * kGolden) ^
-                     static_cast<unsigned long long>(static_cast<long long>(scene->player) * 257);
-        }
+/* The unit's per-origin scalars (computed by every thread that needs them,
+ * so no thread waits for another; `fogged` also evaluates the sky factor). */
+__device__ __forceinline__ void unit_head(UnitHead &h, const tb_sensor_scene *__restrict__ scene, int part,
+                                          bool fogged) {
+    const int scenario = scene->scenario;
+    const bool bwb = is_bwb(scenario), arena = is_arena(scenario);
+    const double qw = scene->attitude[0], qx = scene->attitude[1], qy = scene->attitude[2], qz = scene->attitude[3];
+    h.q[0] = qw;
+    h.q[1] = qx;
+    h.q[2] = qy;
+    h.q[3] = qz;
+    /* Sensor mounts: LiDAR heads sensors.c:32, cameras :72. */
+    Vec mount;
+    if (part < 2) {
+        mount = Vec{0.4, 0.4, part ? -0.4 : 0.4};
+    } else {
+        const int view = (part - 2) >> 1;
+        mount = view < 2 ? Vec{0.42, 0.42, view == 0 ? 0.13 : 0.08} : Vec{0, 0, view == 2 ? -0.5 : 0.5};
     }
-    __syncthreads();
-    if (s.skip) return;
-    /* Spheres in trace order: obstacles, the arena opponent, balls. */
-    const int n = s.n_obstacles + s.arena + s.n_balls;
+    const Vec r = rotate(qw, qx, qy, qz, mount);
+    const double ox = scene->position[0] + r.x, oy = scene->position[1] + r.y, oz = scene->position[2] + r.z;
+    h.origin[0] = ox;
+    h.origin[1] = oy;
+    h.origin[2] = oz;
+    const Vec axis = rotate(qw, qx, qy, qz, Vec{g_cone[part][0], g_cone[part][1], g_cone[part][2]});
+    h.axis[0] = axis.x;
+    h.axis[1] = axis.y;
+    h.axis[2] = axis.z;
+    const double norm2 = qw * qw + qx * qx + qy * qy + qz * qz;
+    h.cull = TB_SENSOR_CULL && fabs(norm2 - 1.0) < 1e-9;
+    const double lidar_max = scene->lidar_max;
+    h.best0 = bwb ? fmax(lidar_max, 120.0) : lidar_max;
+    h.sky_fog = fogged ? fog(h.best0) : 0.0;
+    h.max_range = bwb ? fmax(120.0, lidar_max) : lidar_max;
+    const double dome = bwb ? 300.0 : scene->dome_radius;
+    h.dome_cc = ox * ox + oy * oy - dome * dome;
+    /* Inside the cylinder at horizontal radius rho, a dome hit needs a
+     * horizontal run of at least dome - rho, so t >= dome - rho. */
+    const double rho = sqrt(ox * ox + oy * oy);
+    h.dome = !(TB_SENSOR_CULL && dome - rho > h.best0 * (1 + 1e-9) + 1e-9);
+    h.shelf = scenario == 10;
+    h.arena = arena;
+    h.n_obstacles = min(max(scene->obstacle_count, 0), TB_SENSOR_MAX_OBSTACLES);
+    h.n_balls = min(max(scene->ball_count, 0), TB_SENSOR_MAX_BALLS);
+    /* sensors.c:30: rng ^ step_index * golden ^ player * 257 */
+    h.seed = scene->rng ^ (static_cast<unsigned long long>(static_cast<long long>(scene->step_index)) * kGolden) ^
+             static_cast<unsigned long long>(static_cast<long long>(scene->player) * 257);
+}
+
+/* Forms unit `part` of `scene` in s: the first warps form the scalars and the
+ * sphere list (two CTA barriers in all); every thread returns after the
+ * second, with s complete. */
+__device__ __forceinline__ void prepare_unit(UnitScene &s, const tb_sensor_scene *__restrict__ scene, int part) {
+    const int t = threadIdx.x;
     double ocx = 0, ocy = 0, ocz = 0, occ = 0, rr = 0;
     bool keep = false;
+    int n_obst = 0, arena = 0;
     if (t < 32 * kSphereWarps) {
+        UnitHead h;
+        unit_head(h, scene, part, t == 0);
+        if (t == 0) {
+            s.h = h;
+            s.valid_count = 0;
+            s.warps_done = 0;
+        }
+        /* Spheres in trace order: obstacles, the arena opponent, balls. */
+        n_obst = h.n_obstacles;
+        arena = h.arena;
+        const int n = n_obst + arena + h.n_balls;
         if (t < n) {
             double cx, cy, cz, radius;
-            if (t < s.n_obstacles) {
+            if (t < n_obst) {
                 cx = scene->obstacles[t][0];
                 cy = scene->obstacles[t][1];
                 cz = scene->obstacles[t][2];
                 radius = scene->obstacles[t][3];
-            } else if (s.arena && t == s.n_obstacles) {
+            } else if (arena && t == n_obst) {
                 cx = scene->opponent[0];
                 cy = scene->opponent[1];
                 cz = scene->opponent[2];
                 radius = is_bwb(scene->scenario) ? 0.75 : 0.45;
             } else {
-                const int j = t - s.n_obstacles - s.arena;
+                const int j = t - n_obst - arena;
                 cx = scene->balls[j][0];
                 cy = scene->balls[j][1];
                 cz = scene->balls[j][2];
                 radius = 0.25;
             }
-            ocx = s.origin[0] - cx;
-            ocy = s.origin[1] - cy;
-            ocz = s.origin[2] - cz;
+            ocx = h.origin[0] - cx;
+            ocy = h.origin[1] - cy;
+            ocz = h.origin[2] - cz;
             occ = ocx * ocx + ocy * ocy + ocz * ocz;
             rr = radius * radius;
-            keep = !(s.cull && cone_misses(s, g_cone[part], cx, cy, cz, radius));
+            keep = !(h.cull && cone_misses(h, g_cone[part], cx, cy, cz, radius));
         }
         const unsigned int m = __ballot_sync(0xffffffffu, keep);
-        const unsigned int obst = __ballot_sync(0xffffffffu, keep && t < s.n_obstacles);
-        const unsigned int opp = __ballot_sync(0xffffffffu, keep && s.arena && t == s.n_obstacles);
+        const unsigned int obst = __ballot_sync(0xffffffffu, keep && t < n_obst);
+        const unsigned int opp = __ballot_sync(0xffffffffu, keep && arena && t == n_obst);
         if ((t & 31) == 0) {
             s.keep_mask[t >> 5] = m;
             s.obst_mask[t >> 5] = obst;
@@ -367,31 +378,43 @@ __device__ void prepare_unit(UnitScene &s, const tb_sensor_scene *__restrict__ s
             s.kept_opponent = kept_opp;
         }
     }
+    __syncthreads();
 }
 
 __global__ void __launch_bounds__(kThreads, TB_SENSOR_MIN_BLOCKS)
     sensors_kernel(const tb_sensor_scene *__restrict__ scenes, unsigned long long units, float *__restrict__ lidar,
                    unsigned long long lidar_stride, float *__restrict__ lidar_valid, unsigned long long valid_stride,
                    unsigned char *__restrict__ cameras, unsigned char *__restrict__ raw) {
-    __shared__ UnitScene s;
+    /* Two slots, alternating over the units this CTA renders: a slot is
+     * rewritten only after both barriers of the unit in between, which every
+     * thread passes after it finished tracing from that slot. */
+    __shared__ UnitScene slots[2];
     const int t = threadIdx.x;
+    const bool lidar_out = lidar != nullptr, camera_out = cameras != nullptr || raw != nullptr;
+    int used = 0;
     for (unsigned long long unit = blockIdx.x; unit < units; unit += gridDim.x) {
         const unsigned long long scene_index = unit / kUnitsPerScene;
         const int part = static_cast<int>(unit - scene_index * kUnitsPerScene);
-        __syncthreads(); /* the previous unit is done with s */
-        prepare_unit(s, scenes + scene_index, part, lidar != nullptr, cameras != nullptr || raw != nullptr);
-        if (s.skip) continue; /* CTA-uniform */
-        __syncthreads();
-        const double qw = s.q[0], qx = s.q[1], qy = s.q[2], qz = s.q[3];
+        const tb_sensor_scene *scene = scenes + scene_index;
+        const int sensors = scene->sensors; /* the same word for every thread: a CTA-uniform skip */
+        if (!(part < 2 ? (lidar_out && (sensors & TB_SENSOR_LIDAR)) : (camera_out && (sensors & TB_SENSOR_CAMERA))))
+            continue;
+        UnitScene &s = slots[used & 1];
+        ++used;
+        prepare_unit(s, scene, part);
+        const double qw = s.h.q[0], qx = s.h.q[1], qy = s.h.q[2], qz = s.h.q[3];
 
         if (part < 2) {
             /* LiDAR head `part` (sensors.c:31-49). */
             float *out = lidar + scene_index * lidar_stride;
+            const double max_range = s.h.max_range;
+            /* SplitMix64 state before the draw of bin b is seed + (b + 1) * golden */
+            unsigned long long state = s.h.seed + static_cast<unsigned long long>(part * kUnitRays + t + 1) * kGolden;
             int valid = 0;
 #pragma unroll 1
-            for (int k = 0; k < kUnitRays / kThreads; ++k) {
+            for (int k = 0; k < kUnitRays / kThreads; ++k, state += static_cast<unsigned long long>(kThreads) * kGolden) {
                 const int bin = part * kUnitRays + k * kThreads + t;
-                const unsigned long long hash = splitmix(s.seed + static_cast<unsigned long long>(bin + 1) * kGolden);
+                const unsigned long long hash = splitmix(state);
                 const bool blocked = (g_lidar_blocked[bin >> 5] >> (bin & 31)) & 1u;
                 float value = -1.0f;
                 if (!(static_cast<double>(hash & 0xffff) / 65536.0 < 0.005 || blocked)) {
@@ -399,20 +422,21 @@ __global__ void __launch_bounds__(kThreads, TB_SENSOR_MIN_BLOCKS)
                     int kind;
                     double range = trace(s, rw, kind);
                     const double noise = (static_cast<double>((hash >> 16) & 0xffff) / 32768.0 - 1.0) * 0.02;
-                    range = fmax(0.05, fmin(s.max_range, range + noise));
+                    range = fmax(0.05, fmin(max_range, range + noise));
                     value = static_cast<float>(range);
                     ++valid;
                 }
                 out[bin] = value;
             }
             if (lidar_valid) {
+                /* the last warp to finish writes the head's valid fraction */
                 valid = __reduce_add_sync(0xffffffffu, valid);
-                if ((t & 31) == 0) s.valid[t >> 5] = valid;
-                __syncthreads();
-                if (t == 0) {
-                    int total = 0;
-                    for (int w = 0; w < kWarps; ++w) total += s.valid[w];
-                    lidar_valid[scene_index * valid_stride + part] = static_cast<float>(total) / 2048;
+                if ((t & 31) == 0) {
+                    atomicAdd(&s.valid_count, valid);
+                    __threadfence_block();
+                    if (atomicAdd(&s.warps_done, 1) == kWarps - 1)
+                        lidar_valid[scene_index * valid_stride + part] =
+                            static_cast<float>(atomicAdd(&s.valid_count, 0)) / 2048;
                 }
             }
         } else {
