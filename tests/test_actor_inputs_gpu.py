@@ -106,6 +106,22 @@ def test_argument_rejection():
     assert tb.tb_cuda_prepare_actor_inputs_device(d[0].data_ptr() + 4, d[1], d[2], *outs, n) == 0
 
 
+def test_bounded_pipeline_wait_reports_and_recovers():
+    """An aircraft whose staged copies are withheld makes the bounded waits of
+    the streaming kernel expire: the launch ends, tb_cuda_synchronize reports
+    it once, and the next call is whole and correct."""
+    n = 64
+    obs, mission, cams, _ = tb.generate(44, 0, n)
+    d = [torch.from_numpy(x).cuda() for x in (obs, mission, cams)]
+    outs = _outputs(n)
+    assert tb.take_status() == 0 and tb.tb_cuda_synchronize() == 1
+    assert tb.launch_actor_inputs(*d, outs[2], outs[3], outs[0], outs[1], outs[4], outs[5], n, None,
+                                  wait_ns=20_000_000, stall_sample=5) == 1
+    assert tb.tb_cuda_synchronize() == 0
+    assert tb.tb_cuda_synchronize() == 1          # reported once, then cleared
+    check(obs, mission, cams, "after-timeout")
+
+
 @pytest.mark.skipif(not oracle.have_reference_actor_inputs(), reason="reference GPU build absent")
 def test_faster_than_the_reference_kernels():
     """Records both timings at 65,536 aircraft (CUDA events) and requires this

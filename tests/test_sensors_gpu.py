@@ -151,6 +151,26 @@ def test_sensor_mask_and_null_outputs():
         assert np.array_equal(c[i], want[2][i]) if bits & 2 else (c[i] == 7).all()
 
 
+@pytest.mark.parametrize("count", [1, 3, 17])
+def test_ragged_counts_write_only_their_rows(count):
+    """Small and odd counts render exactly their scenes; rows past count stay
+    untouched."""
+    g = np.load(GOLDEN)
+    scenes = g["scenes"].view(SCENE_DTYPE).reshape(-1)[-count:].copy()
+    scenes["sensors"] = 3
+    n = count + 2
+    d = _scenes_to_device(scenes)
+    lidar = torch.full((n, 4096), -3.0, device=DEV)
+    valid = torch.full((n, 2), -3.0, device=DEV)
+    cams = torch.full((n, 16384), 9, dtype=torch.uint8, device=DEV)
+    assert tb_cuda_render_sensors_device(d, count, lidar, 4096, valid, 2, cams) == 1
+    torch.cuda.synchronize()
+    l, v, c = lidar.cpu().numpy(), valid.cpu().numpy(), cams.cpu().numpy()
+    want = oracle.render_sensors_port(scenes)
+    assert_same((l[:count], v[:count], c[:count], None), (want[0], want[1], want[2], None), f"count {count}")
+    assert (l[count:] == -3).all() and (v[count:] == -3).all() and (c[count:] == 9).all()
+
+
 def test_non_default_stream():
     scenes = synthetic_scenes(11, 64)
     s = torch.cuda.Stream(device=DEV)

@@ -17,14 +17,19 @@
  *   luma[16384]      camera byte / 255 - 0.5
  *
  * Design (B200): the onboard kernel (onboard_kernel.cu) produces tactical
- * and prior; this streaming kernel then reads each aircraft's LiDAR block
- * and cameras once and writes the 6 LiDAR channels and the luma plane with
- * 128-bit streaming stores, every warp store covering 512 contiguous bytes
- * (partial-line stores cost write bandwidth); each thread loads the next
- * aircraft's inputs before storing the current one's.  It moves 33,016
- * bytes in and 115,404 bytes out per aircraft, so it is bound by HBM write
- * bandwidth.  Persistent grid of exactly the resident CTAs, one aircraft per
- * 256-thread CTA iteration.
+ * and prior; this kernel then streams every aircraft once.  It moves 33,016
+ * bytes in and 115,404 bytes out per aircraft, so it is bound by HBM
+ * bandwidth, mostly writes.  Inputs are staged the way the feature kernel
+ * stages them: a producer warp bulk-copies each aircraft's observation row
+ * and camera block (cp.async.bulk, completion counted in bytes on an
+ * mbarrier) and its mission row (4-byte cp.async on the same mbarrier) into
+ * a 3-stage shared-memory ring, so many aircraft are in flight without
+ * holding registers; 8 consumer warps convert a staged aircraft and write
+ * every output with 128-bit streaming stores, each warp store covering 512
+ * contiguous bytes.  Persistent grid of exactly the resident CTAs (2 per SM).
+ * Every mbarrier wait is bounded (about one second); on expiry the kernel
+ * records a status bit that tb_cuda_synchronize() reports, drains its own
+ * outstanding copies (bounded again) and exits.
  *
  * Arithmetic follows the reference kernels' expressions (as nvcc compiles
  * them, i.e. with the multiply-add of the luma contracted), so the values
@@ -36,17 +41,38 @@
 #include <stdint.h>
 
 #include "tb_features_internal.h"
+#include "tb_pipeline.cuh"
 #include "turbinator/training/cuda_features.h"
 
 namespace {
+
+using namespace tb_pipe;
 
 constexpr int kObsDim = 4148;
 constexpr int kMissionDim = 10;
 constexpr int kCameraBytes = 16384;
 constexpr int kProprio = 91;
 constexpr int kMissionVec = 49;
-constexpr int kLidarBins = 2048;          /* per head */
-constexpr int kThreads = 256;
+constexpr int kLidarBins = 2048; /* per head */
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = 32 * kConsumerWarps;
+constexpr int kThreads = kConsumers + 32; /* + the producer warp */
+
+/* Ring geometry: one aircraft per stage (observation row, camera block,
+ * mission row), 3 stages of 33,024 bytes per CTA, 2 CTAs per SM. */
+constexpr uint32_t kObsBytes = kObsDim * 4u; /* 16,592 = 16 * 1,037 */
+constexpr uint32_t kCamOff = kObsBytes;
+constexpr uint32_t kMissionOff = kCamOff + kCameraBytes;
+constexpr uint32_t kStageBytes = (kMissionOff + kMissionDim * 4 + 127) / 128 * 128;
+constexpr int kStages = 3;
+constexpr uint32_t kBarrierRegion = 128;
+constexpr uint32_t kSmemBytes = kBarrierRegion + kStages * kStageBytes;
+static_assert(kObsBytes % 16 == 0 && kCameraBytes % 16 == 0 && kStageBytes == 33024, "stage layout");
+
+constexpr unsigned long long kDefaultWaitNs = 1000000000ull; /* ~1 s per wait */
+
+/* Sticky per-device status word, read and cleared by tb_cuda_synchronize. */
+__device__ unsigned int g_actor_status;
 
 /* Symlog scale of proprioceptive input i (network_gpu.cu:289-295). */
 __device__ __forceinline__ float symlog_scale(int i) {
@@ -83,93 +109,203 @@ __device__ __forceinline__ float4 luma4(uint32_t w) {
     return make_float4(luma(w & 255u), luma((w >> 8) & 255u), luma((w >> 16) & 255u), luma(w >> 24));
 }
 
-/* One aircraft's inputs held in registers: LiDAR float4s q = k*256 + t and
- * camera words c = m*256 + t of this thread. */
-struct RowLoads {
-    float4 lidar[4];
-    uint32_t cam[16];
+struct ActorArgs {
+    const float *obs, *mission;
+    const unsigned char *cameras;
+    const float *tactical, *prior;
+    float *proprio, *mission_vec, *lidar, *luma;
+    unsigned long long batch;
+    unsigned long long wait_ns;
+    long long stall_sample; /* test hook: withhold this aircraft's copies; -1 normally */
 };
 
-__device__ __forceinline__ void load_row(RowLoads &r, const float *o, const unsigned char *cam_row, int t) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) r.lidar[k] = __ldg(reinterpret_cast<const float4 *>(o + 48) + k * kThreads + t);
-    const uint32_t *cw = reinterpret_cast<const uint32_t *>(cam_row);
-#pragma unroll
-    for (int m = 0; m < 16; ++m) r.cam[m] = __ldg(cw + m * kThreads + t);
-}
+__global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const uint32_t full_bar = smem_addr(smem);           /* kStages x 8 B */
+    const uint32_t empty_bar = full_bar + 8 * kStages;   /* kStages x 8 B */
+    unsigned char *stages = smem + kBarrierRegion;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
 
-__global__ void __launch_bounds__(kThreads) actor_inputs_kernel(
-    const float *__restrict__ obs, const float *__restrict__ mission, const unsigned char *__restrict__ cameras,
-    const float *__restrict__ tactical, const float *__restrict__ prior, float *__restrict__ proprio,
-    float *__restrict__ mission_vec, float *__restrict__ lidar, float *__restrict__ luma_out,
-    unsigned long long batch) {
-    const int t = threadIdx.x;
-    unsigned long long b = blockIdx.x;
-    if (b >= batch) return;
-    RowLoads cur;
-    load_row(cur, obs + b * kObsDim, cameras + b * kCameraBytes, t);
-    for (; b < batch; b += gridDim.x) {
-        /* Issue the next aircraft's loads before this one's stores. */
-        const unsigned long long nb = b + gridDim.x;
-        RowLoads nxt;
-        if (nb < batch) load_row(nxt, obs + nb * kObsDim, cameras + nb * kCameraBytes, t);
-        const float *o = obs + b * kObsDim;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full_bar + 8 * s, 1);
+            mbar_init(empty_bar + 8 * s, kConsumerWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
 
-        /* LiDAR: float4 q (0..1023) of the scan is head q/512, bins 4*(q%512)..;
-         * it feeds channels head, 2+head and 4+head.  Each warp store covers
-         * 512 contiguous bytes of one channel row. */
-        float *lo = lidar + b * (6ull * kLidarBins);
+    const unsigned long long first = blockIdx.x;
+    const unsigned long long step = gridDim.x;
+
+    if (warp == kConsumerWarps) {
+        /* ---------------- producer warp ---------------- */
+        const uint64_t policy = evict_first_policy();
+        unsigned long long k = 0;
+        bool ok = true;
+        for (unsigned long long b = first; b < a.batch; b += step, ++k) {
+            const int s = static_cast<int>(k % kStages);
+            const uint32_t phase = static_cast<uint32_t>((k / kStages) & 1);
+            /* warp-uniform: every lane leaves together or none does */
+            if (!__all_sync(0xffffffffu, mbar_wait(empty_bar + 8 * s, phase ^ 1u, a.wait_ns))) {
+                ok = false;
+                break;
+            }
+            if (static_cast<long long>(b) == a.stall_sample) continue; /* test hook */
+            const uint32_t stage = smem_addr(stages + static_cast<size_t>(s) * kStageBytes);
+            if (lane < kMissionDim) {
+                async_load4(stage + kMissionOff + 4 * lane, a.mission + b * kMissionDim + lane);
+                async_track(full_bar + 8 * s);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive_expect_tx(full_bar + 8 * s, kObsBytes + kCameraBytes);
+                bulk_load(stage, a.obs + b * kObsDim, kObsBytes, full_bar + 8 * s, policy);
+                bulk_load(stage + kCamOff, a.cameras + b * kCameraBytes, kCameraBytes, full_bar + 8 * s, policy);
+            }
+            __syncwarp();
+        }
+        if (!ok) {
+            if (lane == 0) atomicOr(&g_actor_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
+            /* Drain this CTA's outstanding copies before exiting (bounded). */
+            const unsigned long long lo = k > kStages ? k - kStages : 0;
+            for (unsigned long long j = lo; j < k; ++j)
+                mbar_wait(full_bar + 8 * (j % kStages), static_cast<uint32_t>((j / kStages) & 1), a.wait_ns);
+        }
+        return;
+    }
+
+    /* ---------------- consumer warps ---------------- */
+    const int t = threadIdx.x; /* 0..255 */
+    unsigned long long k = 0;
+    for (unsigned long long b = first; b < a.batch; b += step, ++k) {
+        const int s = static_cast<int>(k % kStages);
+        const uint32_t phase = static_cast<uint32_t>((k / kStages) & 1);
+        if (!__all_sync(0xffffffffu, mbar_wait(full_bar + 8 * s, phase, a.wait_ns))) {
+            if (lane == 0) atomicOr(&g_actor_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
+            return;
+        }
+        const unsigned char *stage = stages + static_cast<size_t>(s) * kStageBytes;
+        const float *o = reinterpret_cast<const float *>(stage);
+        const float *m = reinterpret_cast<const float *>(stage + kMissionOff);
+
+        /* LiDAR: float4 q (0..1023) of the scan is head q/512, bins
+         * 4*(q%512)..; it feeds channels head, 2+head and 4+head.  Each warp
+         * store covers 512 contiguous bytes of one channel row. */
+        float *lo = a.lidar + b * (6ull * kLidarBins);
+        const float4 *scan = reinterpret_cast<const float4 *>(o + 48);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int q = k * kThreads + t;
+        for (int q4 = 0; q4 < 4; ++q4) {
+            const int q = q4 * kConsumers + t;
             const int head = q >> 9;
             const int bin4 = q & 511;
-            const float4 r = cur.lidar[k];
-            const LidarChannels a = lidar_value(r.x), bb = lidar_value(r.y), c = lidar_value(r.z),
-                                d = lidar_value(r.w);
+            const float4 r = scan[q];
+            const LidarChannels c0 = lidar_value(r.x), c1 = lidar_value(r.y), c2 = lidar_value(r.z),
+                                c3 = lidar_value(r.w);
             __stcs(reinterpret_cast<float4 *>(lo + head * kLidarBins) + bin4,
-                   make_float4(a.inverse, bb.inverse, c.inverse, d.inverse));
+                   make_float4(c0.inverse, c1.inverse, c2.inverse, c3.inverse));
             __stcs(reinterpret_cast<float4 *>(lo + (2 + head) * kLidarBins) + bin4,
-                   make_float4(a.scaled, bb.scaled, c.scaled, d.scaled));
+                   make_float4(c0.scaled, c1.scaled, c2.scaled, c3.scaled));
             __stcs(reinterpret_cast<float4 *>(lo + (4 + head) * kLidarBins) + bin4,
-                   make_float4(a.flag, bb.flag, c.flag, d.flag));
+                   make_float4(c0.flag, c1.flag, c2.flag, c3.flag));
         }
         /* Luma: camera word c (bytes 4c..4c+3) -> output float4 c. */
-        float4 *lu = reinterpret_cast<float4 *>(luma_out + b * kCameraBytes);
+        float4 *lu = reinterpret_cast<float4 *>(a.luma + b * kCameraBytes);
+        const uint32_t *cw = reinterpret_cast<const uint32_t *>(stage + kCamOff);
 #pragma unroll
-        for (int m = 0; m < 16; ++m) __stcs(lu + m * kThreads + t, luma4(cur.cam[m]));
+        for (int w = 0; w < 16; ++w) __stcs(lu + w * kConsumers + t, luma4(cw[w * kConsumers + t]));
 
         /* Scalars (network_gpu.cu:285-302). */
-        float *p = proprio + b * kProprio;
-        float *mv = mission_vec + b * kMissionVec;
+        float *p = a.proprio + b * kProprio;
+        float *mv = a.mission_vec + b * kMissionVec;
         if (t < 52) {
             float raw = t < 48 ? o[t] : o[4144 + t - 48];
             raw = isfinite(raw) ? fmaxf(-1000.0f, fminf(1000.0f, raw)) : 0.0f;
             const float symlog = copysignf(log1pf(fabsf(raw * symlog_scale(t))), raw);
             p[t] = fmaxf(-8.0f, fminf(8.0f, symlog / sqrtf(1.0001f)));
         } else if (t < 52 + kMissionDim) {
-            const float m = mission[b * kMissionDim + (t - 52)];
-            mv[t - 52] = isfinite(m) ? m : 0.0f;
+            const float mm = m[t - 52];
+            mv[t - 52] = isfinite(mm) ? mm : 0.0f;
         } else if (t >= 64 && t < 64 + 24) {
-            const float v = tactical[b * 24 + (t - 64)];
+            const float v = a.tactical[b * 24 + (t - 64)];
             p[52 + (t - 64)] = v;
             mv[10 + (t - 64)] = v;
         } else if (t >= 96 && t < 96 + 15) {
-            const float v = prior[b * 15 + (t - 96)];
+            const float v = a.prior[b * 15 + (t - 96)];
             p[76 + (t - 96)] = v;
             mv[34 + (t - 96)] = v;
         }
-        if (nb < batch) cur = nxt;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar + 8 * s);
     }
 }
 
 constexpr int kMaxDevices = 64;
 int g_sms[kMaxDevices];
-int g_blocks[kMaxDevices]; /* resident CTAs per SM of the streaming kernel */
+int g_blocks[kMaxDevices]; /* resident CTAs per SM */
 
 bool aligned(const void *p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0; }
 
 } /* namespace */
+
+/* Launches the streaming kernel alone (tactical and prior already computed);
+ * opts may be NULL (its wait_ns and stall_sample fields are honoured). */
+extern "C" int tb_actor_inputs_launch(const float *obs, const float *mission, const unsigned char *cameras,
+                                      const float *tactical, const float *prior, float *proprio,
+                                      float *mission_vec, float *lidar, float *luma, size_t batch, void *stream,
+                                      const tb_features_launch_opts *opts) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+    if (!g_sms[dev]) {
+        int sms = 0, blocks = 0;
+        if (cudaFuncSetAttribute(actor_inputs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kSmemBytes)) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, actor_inputs_kernel, kThreads, kSmemBytes) !=
+                cudaSuccess)
+            return 0;
+        g_blocks[dev] = blocks > 0 ? blocks : 1;
+        g_sms[dev] = sms;
+    }
+    ActorArgs a;
+    a.obs = obs;
+    a.mission = mission;
+    a.cameras = cameras;
+    a.tactical = tactical;
+    a.prior = prior;
+    a.proprio = proprio;
+    a.mission_vec = mission_vec;
+    a.lidar = lidar;
+    a.luma = luma;
+    a.batch = batch;
+    a.wait_ns = (opts && opts->wait_ns) ? opts->wait_ns : kDefaultWaitNs;
+    a.stall_sample = opts ? opts->stall_sample : -1;
+    cudaGetLastError(); /* report this launch only */
+    /* persistent: exactly the resident CTAs */
+    unsigned long long grid = static_cast<unsigned long long>(g_sms[dev]) * g_blocks[dev];
+    if (grid > batch) grid = batch;
+    actor_inputs_kernel<<<static_cast<unsigned int>(grid), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(a);
+    return cudaGetLastError() == cudaSuccess;
+}
+
+extern "C" int tb_actor_status_take(void *stream, unsigned int *status) {
+    unsigned int value = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyFromSymbolAsync(&value, g_actor_status, sizeof(value), 0, cudaMemcpyDeviceToHost, s) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return 0;
+    if (value) {
+        static const unsigned int zero = 0;
+        if (cudaMemcpyToSymbolAsync(g_actor_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess)
+            return 0;
+    }
+    if (status) *status = value;
+    return 1;
+}
 
 extern "C" int tb_cuda_prepare_actor_inputs_device(const float *device_obs, const float *device_mission,
                                                    const unsigned char *device_cameras, float *device_proprio_91,
@@ -185,25 +321,10 @@ extern "C" int tb_cuda_prepare_actor_inputs_device(const float *device_obs, cons
         !aligned(device_camera_luma, 16) || !aligned(device_mission, 4) || !aligned(device_proprio_91, 4) ||
         !aligned(device_mission_49, 4))
         return 0;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
-    if (!g_sms[dev]) {
-        int sms = 0, blocks = 0;
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, actor_inputs_kernel, kThreads, 0) != cudaSuccess)
-            return 0;
-        g_blocks[dev] = blocks > 0 ? blocks : 1;
-        g_sms[dev] = sms;
-    }
     if (!tb_cuda_extract_onboard_device(device_obs, device_mission, device_tactical_24, device_prior_15,
                                         batch_size, stream))
         return 0;
-    cudaGetLastError(); /* report this launch only */
-    /* persistent: exactly the resident CTAs */
-    unsigned long long grid = static_cast<unsigned long long>(g_sms[dev]) * g_blocks[dev];
-    if (grid > batch_size) grid = batch_size;
-    actor_inputs_kernel<<<static_cast<unsigned int>(grid), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        device_obs, device_mission, device_cameras, device_tactical_24, device_prior_15, device_proprio_91,
-        device_mission_49, device_lidar_6x2048, device_camera_luma, batch_size);
-    return cudaGetLastError() == cudaSuccess;
+    return tb_actor_inputs_launch(device_obs, device_mission, device_cameras, device_tactical_24, device_prior_15,
+                                  device_proprio_91, device_mission_49, device_lidar_6x2048, device_camera_luma,
+                                  batch_size, stream, nullptr);
 }

@@ -48,6 +48,7 @@
 
 #include "turbinator/training/cuda_features.h"
 #include "tb_features_internal.h"
+#include "tb_pipeline.cuh"
 
 namespace {
 
@@ -90,82 +91,7 @@ constexpr unsigned long long kDefaultWaitNs = 1000000000ull; /* ~1 s per wait */
 /* Sticky per-device status word, read and cleared by tb_cuda_synchronize. */
 __device__ unsigned int g_feature_status;
 
-/* ------------------------------------------------------------------ */
-/* PTX wrappers (sm_90+ forms, valid on sm_100a). */
-
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-/* Bounded wait for the phase with the given parity; false on timeout. */
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
-                                          unsigned long long limit_ns) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    for (;;) {
-        for (int i = 0; i < 32; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > limit_ns) return false;
-    }
-}
-
-/* 1-D bulk copy global -> this CTA's shared memory, completion counted on
- * `bar` in bytes.  src, dst and bytes are multiples of 16. */
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
-                                          uint32_t bar, uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
-        : "memory");
-}
-
-/* 4-byte asynchronous copy (mission entries: rows are only 8-byte aligned). */
-__device__ __forceinline__ void async_load4(uint32_t dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-
-/* Make `bar` track completion of this thread's prior cp.async copies. */
-__device__ __forceinline__ void async_track(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ uint64_t evict_first_policy() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
+using namespace tb_pipe; /* staging primitives, tb_pipeline.cuh */
 
 /* ------------------------------------------------------------------ */
 /* Per-feature arithmetic shared by both kernels. */
@@ -677,9 +603,11 @@ extern "C" int tb_cuda_extract_features_device(const float *device_obs, const fl
 
 extern "C" int tb_cuda_synchronize(void *stream) {
     if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return 0;
-    unsigned int features = 0, onboard = 0;
-    if (!tb_features_status_take(stream, &features) || !tb_onboard_status_take(stream, &onboard)) return 0;
-    return (features | onboard) == 0;
+    unsigned int features = 0, onboard = 0, actor = 0;
+    if (!tb_features_status_take(stream, &features) || !tb_onboard_status_take(stream, &onboard) ||
+        !tb_actor_status_take(stream, &actor))
+        return 0;
+    return (features | onboard | actor) == 0;
 }
 
 /* ---- additive entry point: FP32 cameras ---- */

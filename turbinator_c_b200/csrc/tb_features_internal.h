@@ -63,6 +63,17 @@ int tb_features_status_clear(void *stream);
 /* As tb_features_status_take, for the onboard kernel's own status word. */
 int tb_onboard_status_take(void *stream, unsigned int *status);
 
+/* The learner-input streaming kernel alone (tactical and prior already in
+ * place), as tb_cuda_prepare_actor_inputs_device launches it after the
+ * onboard kernel; opts may be NULL (wait_ns and stall_sample are honoured). */
+int tb_actor_inputs_launch(const float *obs, const float *mission, const unsigned char *cameras,
+                           const float *tactical, const float *prior, float *proprio, float *mission_vec,
+                           float *lidar, float *luma, size_t batch, void *stream,
+                           const tb_features_launch_opts *opts);
+
+/* As tb_features_status_take, for the learner-input kernel's status word. */
+int tb_actor_status_take(void *stream, unsigned int *status);
+
 /* Launch geometry of the staged kernel on the current device. */
 int tb_features_staged_config(int *blocks_per_sm, int *sms, int *smem_bytes, int *threads,
                               int *stages);
