@@ -259,6 +259,57 @@ def time_onboard_reference_cpu(obs, mission, target_s: float):
                       f"{t:.2f} s wall"}
 
 
+def time_config1(stream, dev):
+    """BASELINE config 1 (seed 1, 1,024 aircraft): launch latency.  Its
+    34.4 MB of inputs fit in the 126 MB L2, so device time is reported both
+    L2-resident (back to back) and with L2 flushed before every launch (a
+    256 MiB buffer rewritten), each the median of 20 launches timed with CUDA
+    events; launch-inclusive is host wall time from the call to the stream's
+    completion (median of 20, L2-resident)."""
+    import torch
+
+    n = 1024
+    obs, mission, cams, _ = tb.generate(1, 0, n)
+    d_obs, d_mis, d_cam = (torch.from_numpy(x).to(dev) for x in (obs, mission, cams))
+    out = torch.empty((n, 142), dtype=torch.float32, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    for _ in range(5):
+        assert tb.tb_cuda_extract_features_device(d_obs, d_mis, d_cam, out, n, stream) == 1
+    torch.cuda.synchronize(dev)
+
+    def device_ms(flushed):
+        # all 20 (flush,) event, launch, event groups queued before one sync,
+        # so the events bracket the kernel and not the host's launch latency
+        pairs = []
+        with torch.cuda.stream(stream):
+            for _ in range(20):
+                if flushed:
+                    flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                tb.tb_cuda_extract_features_device(d_obs, d_mis, d_cam, out, n, stream)
+                b.record(stream)
+                pairs.append((a, b))
+        stream.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in pairs)
+
+    resident, flushed = device_ms(False), device_ms(True)
+    host = []
+    for _ in range(20):
+        t0 = time.perf_counter()
+        tb.tb_cuda_extract_features_device(d_obs, d_mis, d_cam, out, n, stream)
+        stream.synchronize()
+        host.append(time.perf_counter() - t0)
+    if tb.tb_cuda_synchronize(stream.cuda_stream) != 1:
+        raise RuntimeError("feature kernel reported a pipeline timeout (config 1)")
+    launch_us = statistics.median(host) * 1e6
+    return {"workload": "config 1: seed 1, 1,024 aircraft, 34.4 MB of inputs (fit in the 126 MB L2)",
+            "device_us_l2_resident": resident * 1e3, "device_us_l2_flushed": flushed * 1e3,
+            "launch_inclusive_us": launch_us, "value_l2_flushed": n / (flushed / 1e3), "unit": UNIT,
+            "timing": "medians of 20; events around each launch; host wall clock call -> stream done",
+            "launches": 5 + 60}
+
+
 def time_sensors(scenes, steps, warmup, stream, dev):
     """Device time per launch of tb_cuda_render_sensors_device over the
     resident scenes (LiDAR, valid fractions and cameras of every scene), and
@@ -528,6 +579,28 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                            "every course scene and 64 balls in every arena scene",
                    **legs, "launches": sum(v["launches"] for v in legs.values())}
 
+    # ---- config 1 latency (1,024 aircraft) and, with several ranks, the final gather
+    config1 = time_config1(stream, dev) if rank == 0 else None
+    gather = None
+    if world > 1:
+        import torch.distributed as dist
+
+        gathered = torch.empty((world * count, 142), dtype=torch.float32, device=dev)
+        host_all = torch.empty((world * count, 142), dtype=torch.float32, pin_memory=True) if rank == 0 else None
+        barrier()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        dist.all_gather_into_tensor(gathered, d_out)
+        if rank == 0:
+            host_all.copy_(gathered)
+        torch.cuda.synchronize(dev)
+        g_s = max_over_ranks(time.perf_counter() - t0)
+        gather = {"ms": g_s * 1e3, "bytes_to_host": world * count * tb.FEATURE_DIM * 4,
+                  "op": "NCCL all_gather_into_tensor of every rank's [n,142] slice, then one "
+                        "device-to-host copy of all of them on rank 0 (host wall clock, max over ranks)",
+                  "note": "after the timed region; the kernel-only value above excludes it"}
+        del gathered, host_all
+
     # ---- e2e: the reference-facing host ABI on page-locked host buffers
     e2e_steps = args.e2e_steps or min(args.steps, 20)
     out_host = torch.empty((count, 142), dtype=torch.float32, pin_memory=True).numpy()
@@ -606,12 +679,13 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                      "kernel": "features_staged_kernel", "avg_launch_ms": avg_launch_s * 1e3},
         "gpu_launches": (args.steps + e2e_steps * chunks + (onboard["launches"] if onboard else 0) +
                          (f32cam["launches"] if f32cam else 0) + (actor["launches"] if actor else 0) +
-                         (sensors["launches"] if sensors else 0)),
+                         (sensors["launches"] if sensors else 0) + (60 if config1 else 0)),
         "gpu_launches_detail": {"value_region": args.steps, "e2e_region": e2e_steps * chunks,
                                 "onboard_regions": onboard["launches"] if onboard else 0,
                                 "f32cam_region": f32cam["launches"] if f32cam else 0,
                                 "actor_inputs_region": actor["launches"] if actor else 0,
-                                "sensors_regions": sensors["launches"] if sensors else 0},
+                                "sensors_regions": sensors["launches"] if sensors else 0,
+                                "config1_region": 60 if config1 else 0},
         "clocks": clk,
     }
     if f32cam is not None:
@@ -622,6 +696,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         line["onboard"] = onboard
     if sensors is not None:
         line["sensors"] = sensors
+    if config1 is not None:
+        line["config1_latency"] = config1
+    if gather is not None:
+        line["gather"] = gather
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = time_reference_cpu(obs, mission, cams, args.cpu_seconds)
         if onboard is not None:

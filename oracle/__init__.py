@@ -349,3 +349,29 @@ def simulate_sensor_scenes(scenarios, seeds, steps, players, scene_dtype):
                                           _addr(lidar), _addr(valid), _addr(cams)) != 0:
         raise RuntimeError("reference simulation failed")
     return scenes, lidar, valid, cams
+
+
+# ---- the reference's own GPU feature path (src/cuda/features.cu for sm_100a) ----
+
+REF_CUDA_FEATURES_PATH = os.path.join(HERE, "_ref", "libtb_ref_cuda_features.so")
+_ref_cuda_features = None
+
+
+def have_reference_gpu_features() -> bool:
+    return os.path.exists(REF_CUDA_FEATURES_PATH)
+
+
+def ref_cuda_features() -> ctypes.CDLL:
+    """The reference's GPU feature library, loaded privately (RTLD_LOCAL): its
+    symbols carry the same names as this repository's library."""
+    global _ref_cuda_features
+    if _ref_cuda_features is None:
+        if not have_reference_gpu_features():
+            raise RuntimeError(f"{REF_CUDA_FEATURES_PATH} missing (reference build not available)")
+        l = ctypes.CDLL(REF_CUDA_FEATURES_PATH, mode=ctypes.RTLD_LOCAL)
+        l.tb_cuda_extract_features_device.restype = ctypes.c_int
+        l.tb_cuda_extract_features_device.argtypes = [_vp, _vp, _vp, _vp, _sz, _vp]
+        l.tb_cuda_synchronize.restype = ctypes.c_int
+        l.tb_cuda_synchronize.argtypes = [_vp]
+        _ref_cuda_features = l
+    return _ref_cuda_features
