@@ -194,9 +194,14 @@ def time_reference_cpu(obs, mission, cams, target_s: float):
     while passes == 0 or spent < 0.5 * target_s:
         spent += timed(obs[:sample], mission[:sample], cams[:sample], out[:sample], threads)
         passes += 1
+    # the same function on one thread, over a smaller leading sample
+    one_sample = int(min(n, max(256, rate / max(threads, 1) * target_s / 4)))
+    one_t = timed(obs[:one_sample], mission[:one_sample], cams[:one_sample], out[:one_sample], 1)
     return {"value": sample * passes / spent, "unit": UNIT, "cores": threads, "kind": kind,
             "sample": f"first {sample} of the {n}-aircraft batch x {passes} pass(es), {threads} threads "
-                      f"over contiguous ranges, {spent:.2f} s wall; host CPU: {cpu_description()}"}
+                      f"over contiguous ranges, {spent:.2f} s wall; host CPU: {cpu_description()}",
+            "single_thread": {"value": one_sample / one_t, "unit": UNIT, "cores": 1,
+                              "sample": f"first {one_sample} aircraft, {one_t:.2f} s wall"}}
 
 
 def scanning_fraction(mission) -> float:

@@ -95,6 +95,31 @@ tb_cuda_feature_batch *tb_cuda_feature_batch_create_multi(const int *device_ids,
                                                           int device_count,
                                                           size_t max_batch);
 
+/* Largest shard_count accepted by tb_cuda_extract_features_device_sharded. */
+#define TB_CUDA_MAX_SHARDS 64
+
+/* The device entry point over several GPUs in one call (no counterpart in the
+ * reference, which launches on one device per call).  Shard i is
+ * tb_cuda_extract_features_device(device_obs[i], device_mission[i],
+ * device_cameras ? device_cameras[i] : NULL, device_features[i],
+ * batch_sizes[i], streams ? streams[i] : NULL) run with device_ids[i] current;
+ * every pointer of shard i is memory of that device.  A shard with batch size
+ * 0 launches nothing; an id may repeat.  The calling thread's current device
+ * is restored before returning.  Returns 1 if every launch succeeded; 0 on
+ * shard_count outside 1..TB_CUDA_MAX_SHARDS, a NULL array, an unknown device,
+ * a NULL pointer of a non-empty shard, a batch size > 0x7fffffff, or a launch
+ * error (shards before the failing one may have launched).  Asynchronous:
+ * synchronize each shard's stream on its device (tb_cuda_synchronize with
+ * that device current) before reading its features. */
+int tb_cuda_extract_features_device_sharded(int shard_count,
+                                            const int *device_ids,
+                                            const float *const *device_obs,
+                                            const float *const *device_mission,
+                                            const unsigned char *const *device_cameras,
+                                            float *const *device_features,
+                                            const size_t *batch_sizes,
+                                            void *const *streams);
+
 /* Onboard tactical (24) and physics-prior (15) values per aircraft: the
  * reference's device-only src/network/onboard_features.cuh:515-519
  * (tb_onboard_tactical_prior), which its 618M learner evaluates one thread

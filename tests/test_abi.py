@@ -44,6 +44,11 @@ def test_argument_rejection_without_device():
     assert tb.tb_cuda_extract_features_host(None, fake, fake, fake, 1, fake) == 0
     assert tb.tb_cuda_feature_batch_create(0, 0) is None
     tb.tb_cuda_feature_batch_destroy(None)  # NULL-safe
+    sharded = tb.tb_cuda_extract_features_device_sharded
+    assert sharded([], [], [], None, [], []) == 0                       # no shards
+    assert sharded([0] * 65, [fake] * 65, [fake] * 65, None, [fake] * 65, [1] * 65) == 0  # too many
+    lib = tb.load_library()
+    assert lib.tb_cuda_extract_features_device_sharded(1, None, None, None, None, None, None, None) == 0
     from turbinator_c_b200.sensors import tb_cuda_render_sensors_device as render
     assert render(None, 4, fake, 4096, fake, 2, fake) == 0
     assert render(fake, 0, fake, 4096, fake, 2, fake) == 0

@@ -239,6 +239,51 @@ def test_multi_device_handle_on_distinct_gpus():
             check_features(out[:count], expected[:count], f"distinct GPUs {devices} count={count}")
 
 
+def test_sharded_device_entry_point():
+    """tb_cuda_extract_features_device_sharded: contiguous slices of one batch
+    as shards (here all on device 0, one of them empty), each with its own
+    pointers and stream; the caller's current device is kept."""
+    n = 3001
+    obs, mission, cams, _ = tb.generate(34, 0, n)
+    expected = oracle.features(obs, mission, cams)
+    d_obs, d_mis, d_cam = _dev(obs), _dev(mission), _dev(cams)
+    out = torch.full((n, 142), float("nan"), device="cuda")
+    cuts = [0, 1000, 1000, 2999, n]
+    sl = lambda t, i: t[cuts[i]:cuts[i + 1]]
+    streams = [torch.cuda.Stream() for _ in range(4)]
+    assert tb.tb_cuda_extract_features_device_sharded(
+        [0] * 4, [sl(d_obs, i) for i in range(4)], [sl(d_mis, i) for i in range(4)],
+        [sl(d_cam, i) for i in range(4)], [sl(out, i) for i in range(4)],
+        [cuts[i + 1] - cuts[i] for i in range(4)], streams) == 1
+    assert torch.cuda.current_device() == 0
+    for s in streams:
+        assert tb.tb_cuda_synchronize(s.cuda_stream) == 1
+    check_features(out.cpu().numpy(), expected, "sharded")
+    # rejected: unknown device, NULL pointer of a non-empty shard
+    assert tb.tb_cuda_extract_features_device_sharded([10_000], [d_obs], [d_mis], None, [out], [n]) == 0
+    assert tb.tb_cuda_extract_features_device_sharded([0], [None], [d_mis], None, [out], [n]) == 0
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_sharded_device_entry_point_on_distinct_gpus():
+    devices = list(range(torch.cuda.device_count()))
+    n = 4099
+    obs, mission, cams, _ = tb.generate(35, 0, n)
+    expected = oracle.features(obs, mission, cams)
+    from turbinator_c_b200.shard import shard_range
+    ranges = [shard_range(n, r, len(devices)) for r in range(len(devices))]
+    ins = [[torch.from_numpy(x[f:f + c]).to(f"cuda:{d}") for x in (obs, mission, cams)]
+           for d, (f, c) in zip(devices, ranges)]
+    outs = [torch.full((c, 142), float("nan"), device=f"cuda:{d}") for d, (f, c) in zip(devices, ranges)]
+    assert tb.tb_cuda_extract_features_device_sharded(devices, [i[0] for i in ins], [i[1] for i in ins],
+                                                      [i[2] for i in ins], outs, [c for _, c in ranges]) == 1
+    for d in devices:
+        with torch.cuda.device(d):
+            assert tb.tb_cuda_synchronize(None) == 1
+    got = np.concatenate([o.cpu().numpy() for o in outs])
+    check_features(got, expected, f"sharded over {devices}")
+
+
 def test_multi_device_handle_rejects_bad_devices():
     assert tb.tb_cuda_feature_batch_create_multi([0, 10_000], 16) is None
     assert tb.tb_cuda_feature_batch_create_multi([], 16) is None

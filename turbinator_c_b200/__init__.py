@@ -87,6 +87,8 @@ def load_library() -> ctypes.CDLL:
     _bind(lib, "tb_cuda_extract_features_device_f32cam", _c.c_int, [_vp, _vp, _vp, _vp, _sz, _vp])
     _bind(lib, "tb_cuda_prepare_actor_inputs_device", _c.c_int, [_vp] * 9 + [_sz, _vp])
     _bind(lib, "tb_cuda_render_sensors_device", _c.c_int, [_vp, _sz, _vp, _sz, _vp, _sz, _vp, _vp, _vp])
+    _bind(lib, "tb_cuda_extract_features_device_sharded", _c.c_int,
+          [_c.c_int, _c.POINTER(_c.c_int)] + [_c.POINTER(_vp)] * 4 + [_c.POINTER(_sz), _c.POINTER(_vp)])
     _bind(lib, "tb_actor_inputs_launch", _c.c_int, [_vp] * 9 + [_sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_launch_f32cam", _c.c_int,
           [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
@@ -180,6 +182,18 @@ def tb_cuda_extract_onboard_device(obs, mission, tactical_24, prior_15, batch_si
     """Onboard tactical [B,24] and prior [B,15] values (device pointers)."""
     return load_library().tb_cuda_extract_onboard_device(
         _ptr(obs), _ptr(mission), _ptr(tactical_24), _ptr(prior_15), batch_size, _stream_handle(stream))
+
+
+def tb_cuda_extract_features_device_sharded(device_ids, obs, mission, cameras, features, batch_sizes,
+                                            streams=None) -> int:
+    """Per-shard lists (device ids, device tensors or pointers, batch sizes,
+    optional streams); cameras may be None or a list with None entries."""
+    n = len(device_ids)
+    arr = lambda xs: (_vp * n)(*[_ptr(x) for x in xs])
+    cams = None if cameras is None else arr(cameras)
+    st = None if streams is None else (_vp * n)(*[_stream_handle(x) for x in streams])
+    return load_library().tb_cuda_extract_features_device_sharded(
+        n, (_c.c_int * n)(*device_ids), arr(obs), arr(mission), cams, arr(features), (_sz * n)(*batch_sizes), st)
 
 
 #: Largest count accepted by tb_cuda_extract_features_host_noalloc (cuda_features.h).
