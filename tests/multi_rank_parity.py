@@ -1,8 +1,11 @@
-"""Config-3 parity across ranks (run by tests/test_multi_rank_gpu.py under
-torchrun, one process per GPU, NCCL):
+"""Config-3 and config-4 parity across ranks (run by tests/test_multi_rank_gpu.py
+under torchrun, one process per GPU, NCCL):
 
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
-        --master-port P tests/multi_rank_parity.py [total]
+        --master-port P tests/multi_rank_parity.py [total [config3|config4]]
+
+Config 4 (seed 4, 131,072 aircraft in four stress quarters) is checked in
+full: every rank compares its whole shard with the CPU oracle.
 
 BASELINE config 3 is seed 3 and 524,288 aircraft split into contiguous
 slices of B/N.  Each rank generates only its own slice, extracts it on its
@@ -32,11 +35,13 @@ import turbinator_c_b200 as tb  # noqa: E402
 from tests.parity import check_features  # noqa: E402
 from turbinator_c_b200.shard import gather_features, shard_range  # noqa: E402
 
-SEED = 3
+SEEDS = {"config3": 3, "config4": 4}
 
 
 def main() -> int:
     total = int(sys.argv[1]) if len(sys.argv) > 1 else 524288
+    mode = sys.argv[2] if len(sys.argv) > 2 else "config3"
+    seed, stress = SEEDS[mode], mode == "config4"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -44,19 +49,27 @@ def main() -> int:
     ok = True
     try:
         first, count = shard_range(total, rank, world)
-        obs, mission, cams, _ = tb.generate(SEED, first, count, total=total)
+        obs, mission, cams, _ = tb.generate(seed, first, count, total=total, stress=stress)
         d = [torch.from_numpy(x).cuda() for x in (obs, mission, cams)]
         out = torch.empty((count, 142), device="cuda")
         assert tb.tb_cuda_extract_features_device(*d, out, count, None) == 1
         assert tb.tb_cuda_synchronize(None) == 1
-        full = gather_features(out.cpu().numpy(), total)
-        if rank == 0:
+        mine = out.cpu().numpy()
+        if stress:
+            try:
+                check_features(mine, oracle.features(obs, mission, cams), f"config 4 rank {rank} of {world}")
+                print(f"config 4: rank {rank} of {world}, all {count} aircraft match the oracle")
+            except AssertionError as e:
+                print(f"config 4 mismatch on rank {rank}: {e}")
+                ok = False
+        full = gather_features(mine, total)
+        if rank == 0 and not stress:
             idx = set(range(0, total, 97))
             for r in range(world):
                 f, c = shard_range(total, r, world)
                 idx.update((f, f + c - 1))
             idx = np.array(sorted(idx))
-            rows = [tb.generate(SEED, int(i), 1, total=total) for i in idx]
+            rows = [tb.generate(seed, int(i), 1, total=total) for i in idx]
             o = np.concatenate([r[0] for r in rows])
             m = np.concatenate([r[1] for r in rows])
             cam = np.concatenate([r[2] for r in rows])

@@ -19,12 +19,23 @@ pytestmark = [pytest.mark.gpu,
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def test_config3_parity_across_ranks():
+def _run(total: int, mode: str, port_offset: int):
     n = min(torch.cuda.device_count(), 8)
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           f"--nproc-per-node={n}", "--master-addr", "127.0.0.1", "--master-port", str(29600 + os.getpid() % 200),
-           os.path.join(ROOT, "tests", "multi_rank_parity.py"), "524288"]
+           f"--nproc-per-node={n}", "--master-addr", "127.0.0.1",
+           "--master-port", str(29600 + port_offset + os.getpid() % 100),
+           os.path.join(ROOT, "tests", "multi_rank_parity.py"), str(total), mode]
     run = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
     print(run.stdout[-2000:])
     assert run.returncode == 0, run.stdout[-4000:] + run.stderr[-4000:]
     assert "match the oracle" in run.stdout
+    return run.stdout
+
+
+def test_config3_parity_across_ranks():
+    _run(524288, "config3", 0)
+
+
+def test_config4_full_parity_across_ranks():
+    out = _run(131072, "config4", 100)
+    assert out.count("all ") >= 1
