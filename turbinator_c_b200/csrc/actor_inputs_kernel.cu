@@ -22,8 +22,8 @@
  * bandwidth, mostly writes.  Inputs are staged the way the feature kernel
  * stages them: a producer warp bulk-copies each aircraft's observation row
  * and camera block (cp.async.bulk, completion counted in bytes on an
- * mbarrier) and its mission row (4-byte cp.async on the same mbarrier) into
- * a 3-stage shared-memory ring, so many aircraft are in flight without
+ * mbarrier) and its mission, tactical and prior rows (4-byte cp.async on the
+ * same mbarrier) into a 3-stage shared-memory ring, so many aircraft are in flight without
  * holding registers; 8 consumer warps convert a staged aircraft and write
  * every output with 128-bit streaming stores, each warp store covering 512
  * contiguous bytes.  Persistent grid of exactly the resident CTAs (2 per SM).
@@ -59,15 +59,18 @@ constexpr int kConsumers = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumers + 32; /* + the producer warp */
 
 /* Ring geometry: one aircraft per stage (observation row, camera block,
- * mission row), 3 stages of 33,024 bytes per CTA, 2 CTAs per SM. */
+ * mission row, tactical and prior rows), 3 stages of 33,280 bytes per CTA,
+ * 2 CTAs per SM. */
 constexpr uint32_t kObsBytes = kObsDim * 4u; /* 16,592 = 16 * 1,037 */
 constexpr uint32_t kCamOff = kObsBytes;
 constexpr uint32_t kMissionOff = kCamOff + kCameraBytes;
-constexpr uint32_t kStageBytes = (kMissionOff + kMissionDim * 4 + 127) / 128 * 128;
+constexpr uint32_t kTacticalOff = kMissionOff + kMissionDim * 4;
+constexpr uint32_t kPriorOff = kTacticalOff + 24 * 4;
+constexpr uint32_t kStageBytes = (kPriorOff + 15 * 4 + 127) / 128 * 128;
 constexpr int kStages = 3;
 constexpr uint32_t kBarrierRegion = 128;
 constexpr uint32_t kSmemBytes = kBarrierRegion + kStages * kStageBytes;
-static_assert(kObsBytes % 16 == 0 && kCameraBytes % 16 == 0 && kStageBytes == 33024, "stage layout");
+static_assert(kObsBytes % 16 == 0 && kCameraBytes % 16 == 0 && kStageBytes == 33280, "stage layout");
 
 constexpr unsigned long long kDefaultWaitNs = 1000000000ull; /* ~1 s per wait */
 
@@ -154,10 +157,11 @@ __global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorAr
             }
             if (static_cast<long long>(b) == a.stall_sample) continue; /* test hook */
             const uint32_t stage = smem_addr(stages + static_cast<size_t>(s) * kStageBytes);
-            if (lane < kMissionDim) {
-                async_load4(stage + kMissionOff + 4 * lane, a.mission + b * kMissionDim + lane);
-                async_track(full_bar + 8 * s);
-            }
+            /* the 4-byte-aligned rows: mission, tactical, prior (49 floats) */
+            if (lane < kMissionDim) async_load4(stage + kMissionOff + 4 * lane, a.mission + b * kMissionDim + lane);
+            if (lane < 24) async_load4(stage + kTacticalOff + 4 * lane, a.tactical + b * 24 + lane);
+            if (lane < 15) async_load4(stage + kPriorOff + 4 * lane, a.prior + b * 15 + lane);
+            if (lane < 24) async_track(full_bar + 8 * s);
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive_expect_tx(full_bar + 8 * s, kObsBytes + kCameraBytes);
@@ -228,11 +232,11 @@ __global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorAr
             const float mm = m[t - 52];
             mv[t - 52] = isfinite(mm) ? mm : 0.0f;
         } else if (t >= 64 && t < 64 + 24) {
-            const float v = a.tactical[b * 24 + (t - 64)];
+            const float v = reinterpret_cast<const float *>(stage + kTacticalOff)[t - 64];
             p[52 + (t - 64)] = v;
             mv[10 + (t - 64)] = v;
         } else if (t >= 96 && t < 96 + 15) {
-            const float v = a.prior[b * 15 + (t - 96)];
+            const float v = reinterpret_cast<const float *>(stage + kPriorOff)[t - 96];
             p[76 + (t - 96)] = v;
             mv[34 + (t - 96)] = v;
         }
