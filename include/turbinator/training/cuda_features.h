@@ -39,9 +39,10 @@ int tb_cuda_extract_features_device(const float *device_obs,
                                     void *stream);
 
 /* Replaces cuda_features.h:20 (features.cu:171-173).  Returns 1 when the
- * stream drained without error.  It also returns 0 (once) when a feature
- * kernel on the current device gave up waiting on its staging pipeline;
- * such a launch leaves its features incomplete. */
+ * stream drained without error.  It also returns 0 (once) when a kernel of
+ * this library on the current device (features, onboard values or learner
+ * inputs) gave up waiting on its staging pipeline; such a launch leaves its
+ * outputs incomplete. */
 int tb_cuda_synchronize(void *stream);
 
 typedef struct tb_cuda_feature_batch tb_cuda_feature_batch;
