@@ -47,6 +47,7 @@ SEED = 2
 FALLBACK_HBM_GBS = 6650.0
 PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "features_staged_kernel_traffic.txt")
 SENSOR_SCENES = 32768
+SENSOR_PROFILE = os.path.join(ROOT, "profiles", "sensors_kernel_pipes.txt")
 RAYS_PER_SCENE = 4096 + 16384
 
 
@@ -262,6 +263,21 @@ def time_onboard_reference_cpu(obs, mission, target_s: float):
     return {"value": sample / t, "unit": UNIT, "cores": threads, "kind": "reference",
             "sample": f"first {sample} aircraft, reference onboard header (glibc build), {threads} threads, "
                       f"{t:.2f} s wall"}
+
+
+def profiled_sensor_pipes():
+    """FP64-pipe and issue fractions of the sensor kernel from the committed
+    ncu summary (name -> fraction), or {} if it is missing."""
+    out = {}
+    try:
+        with open(SENSOR_PROFILE) as f:
+            for line in f:
+                if ":" in line and not line.startswith("#"):
+                    k, v = line.split(":", 1)
+                    out[k.strip()] = float(v)
+    except (OSError, ValueError):
+        pass
+    return out
 
 
 def time_config1(stream, dev):
@@ -576,7 +592,14 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                                   "api": "scenes copied in from page-locked memory, LiDAR + valid + cameras "
                                          "copied back, every step (host wall clock)"},
                           "launches": s_steps + max(1, min(s_steps, 5))}
+        pipes = profiled_sensor_pipes()
         sensors = {"entry_point": "tb_cuda_render_sensors_device",
+                   "roofline": {"bound": "fp64 pipe / instruction issue (not HBM, not tensor)",
+                                "fp64_pipe_frac": {"flight_mix": pipes.get("fp64_pipe_frac_flight_mix"),
+                                                   "heaviest": pipes.get("fp64_pipe_frac_heaviest")},
+                                "issue_active_frac": {"flight_mix": pipes.get("issue_active_frac_flight_mix"),
+                                                      "heaviest": pipes.get("issue_active_frac_heaviest")},
+                                "source": "ncu --set full of 4,096 scenes (profiles/sensors_kernel_s4096.md)"},
                    "outputs": "4,096 LiDAR ranges + 2 valid fractions + 4 x 64 x 64 camera bytes per scene",
                    "bound": "FP64 pipe (double-precision ray/sphere tests, no FMA contraction), not HBM",
                    "data": "synthetic scenes with the simulator's geometry (seeded); flight_mix: uniform over "
