@@ -20,8 +20,11 @@
  *    rounding.
  *  - Only aircraft whose mission reads the scans (dodge, slalom) are
  *    scanned; a CTA lists them per chunk of 512 aircraft and deals them to
- *    its warps round-robin.  The scalar control law then runs one aircraft
- *    per thread.
+ *    its warps round-robin (onboard_scan_kernel, one CTA per SM for its
+ *    shared-memory staging).  The scalar control law runs in a second launch,
+ *    one aircraft per thread without shared memory (onboard_control_kernel),
+ *    so a 65,536-aircraft batch is one wave; a scanned aircraft's results
+ *    reach it parked in its own prior row.
  *  - Ray directions (12 elevation and 128 azimuth cosines/sines) are built
  *    once per CTA in shared memory.
  *
@@ -830,24 +833,54 @@ __device__ void prior(const float *o, const float *m, const RayStats &rs, float 
 }
 
 /* ------------------------------------------------------------------ */
-/* Persistent: one CTA per SM; each CTA owns a balanced contiguous range of
- * aircraft and walks it kChunk at a time.  Per chunk: (1) the aircraft whose
- * mission reads the LiDAR scans (dodge: nearest return; slalom: corridor)
- * are listed in shared memory; (2) the warps take those scan jobs
- * round-robin, each staging the next job's LiDAR block with bulk copies
- * while it scans the current one, and leave the results in shared memory;
- * (3) every thread runs the control law for one aircraft at a time. */
+/* Two launches.  (1) onboard_scan_kernel, persistent with one CTA per SM:
+ * each CTA owns a balanced contiguous range of aircraft and walks it kChunk
+ * at a time; the aircraft whose mission reads the LiDAR scans (dodge:
+ * nearest return; slalom: corridor) are listed in shared memory and the
+ * warps take those scan jobs round-robin, each staging the next job's LiDAR
+ * block with bulk copies while it scans the current one.  A scanned
+ * aircraft's RayStats go to the first six floats of its own prior row, which
+ * the second launch reads back before overwriting the row.  (2)
+ * onboard_control_kernel runs the control law, one aircraft per thread, with
+ * no shared memory, so every aircraft of a 65,536 batch is in one wave. */
 struct ChunkState {
-    RayStats stats[kChunk];
     unsigned short jobs[kChunk];   /* aircraft index in chunk | 0x4000 near | 0x8000 corridor */
     int job_count;
 };
 
-__global__ void __launch_bounds__(kThreads) onboard_kernel(const float *__restrict__ obs,
-                                                           const float *__restrict__ mission,
-                                                           float *__restrict__ tactical_out,
-                                                           float *__restrict__ prior_out,
-                                                           unsigned long long batch) {
+/* The missions that read the scans (onboard_features.cuh:201-239). */
+__device__ __forceinline__ void scan_modes(const float *mrow, bool &dodge, bool &slalom) {
+    const float m4 = mission_value(__ldg(mrow + 4));
+    const float m5 = mission_value(__ldg(mrow + 5));
+    dodge = m5 > 0.75f;
+    slalom = m4 > 0.75f && !(m4 > 0.75f && m5 > 0.25f);
+}
+
+/* RayStats parked in a prior row between the two launches (24 of its 60 bytes). */
+__device__ __forceinline__ void park_stats(float *row, const RayStats &st) {
+    row[0] = st.min_r;
+    row[1] = st.min_r_dx;
+    row[2] = st.min_r_dy;
+    row[3] = st.min_dx_c;
+    row[4] = st.cluster_y_sum;
+    row[5] = __int_as_float(st.cluster_count);
+}
+
+__device__ __forceinline__ RayStats unpark_stats(const float *row) {
+    RayStats st;
+    st.min_r = row[0];
+    st.min_r_dx = row[1];
+    st.min_r_dy = row[2];
+    st.min_dx_c = row[3];
+    st.cluster_y_sum = row[4];
+    st.cluster_count = __float_as_int(row[5]);
+    return st;
+}
+
+__global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__restrict__ obs,
+                                                                const float *__restrict__ mission,
+                                                                float *__restrict__ prior_out,
+                                                                unsigned long long batch) {
     __shared__ RayTables tables;
     extern __shared__ __align__(128) unsigned char dyn[];
     build_ray_tables(tables);
@@ -879,17 +912,8 @@ __global__ void __launch_bounds__(kThreads) onboard_kernel(const float *__restri
         __syncthreads();
         /* (1) scan jobs of this chunk */
         for (int i = threadIdx.x; i < n; i += kThreads) {
-            RayStats &st = chunk.stats[i];
-            st.min_r = 30.0f;
-            st.min_r_dx = 0.0f;
-            st.min_r_dy = 0.0f;
-            st.min_dx_c = 30.0f;
-            st.cluster_y_sum = 0.0f;
-            st.cluster_count = 0;
-            const float m4 = mission_value(__ldg(mission + (first + i) * kMissionDim + 4));
-            const float m5 = mission_value(__ldg(mission + (first + i) * kMissionDim + 5));
-            const bool dodge = m5 > 0.75f;
-            const bool slalom = m4 > 0.75f && !(m4 > 0.75f && m5 > 0.25f);
+            bool dodge, slalom;
+            scan_modes(mission + (first + i) * kMissionDim, dodge, slalom);
             if (dodge || slalom)
                 chunk.jobs[atomicAdd(&chunk.job_count, 1)] =
                     static_cast<unsigned short>(i | (dodge ? 0x4000 : 0) | (slalom ? 0x8000 : 0));
@@ -920,33 +944,53 @@ __global__ void __launch_bounds__(kThreads) onboard_kernel(const float *__restri
                                              obs_value(__ldg(row + 8)), obs_value(__ldg(row + 9)));
             const RayStats st = scan_rays(tables, slot, slot.ranges[seq & 1], a, obs_value(__ldg(row + 1)),
                                           cos_az, sin_az, lane, (job & 0x4000) != 0, (job & 0x8000) != 0);
-            if (lane == 0) chunk.stats[i] = st;
+            if (lane == 0) park_stats(prior_out + (first + i) * 15, st);
             ++seq;
         }
-        __syncthreads();
-        /* (3) control law, one aircraft per thread */
-        for (int i = threadIdx.x; i < n; i += kThreads) {
-            const unsigned long long sample = first + i;
-            const float *row = obs + sample * kObsDim;
-            const float *mrow = mission + sample * kMissionDim;
-            float raw_o[48], raw_m[10], o[48], m[10];
-            for (int k = 0; k < 48; ++k) {
-                raw_o[k] = __ldg(row + k);
-                o[k] = obs_value(raw_o[k]);
-            }
-            for (int k = 0; k < 10; ++k) {
-                raw_m[k] = __ldg(mrow + k);
-                m[k] = mission_value(raw_m[k]);
-            }
-            tactical(raw_o, raw_m, tactical_out + sample * 24);
-            prior(o, m, chunk.stats[i], prior_out + sample * 15);
-        }
-        __syncthreads();
+        __syncthreads(); /* the job list is rewritten by the next chunk */
     }
 }
 
+constexpr int kControlThreads = 128;
+
+__global__ void __launch_bounds__(kControlThreads) onboard_control_kernel(const float *__restrict__ obs,
+                                                                          const float *__restrict__ mission,
+                                                                          float *__restrict__ tactical_out,
+                                                                          float *__restrict__ prior_out,
+                                                                          unsigned long long batch) {
+    const unsigned long long sample = static_cast<unsigned long long>(blockIdx.x) * kControlThreads + threadIdx.x;
+    if (sample >= batch) return;
+    const float *row = obs + sample * kObsDim;
+    const float *mrow = mission + sample * kMissionDim;
+    bool dodge, slalom;
+    scan_modes(mrow, dodge, slalom);
+    RayStats st;
+    if (dodge || slalom) {
+        st = unpark_stats(prior_out + sample * 15);
+    } else {
+        /* the reference's initial values (onboard_features.cuh:188-199) */
+        st.min_r = 30.0f;
+        st.min_r_dx = 0.0f;
+        st.min_r_dy = 0.0f;
+        st.min_dx_c = 30.0f;
+        st.cluster_y_sum = 0.0f;
+        st.cluster_count = 0;
+    }
+    float raw_o[48], raw_m[10], o[48], m[10];
+    for (int k = 0; k < 48; ++k) {
+        raw_o[k] = __ldg(row + k);
+        o[k] = obs_value(raw_o[k]);
+    }
+    for (int k = 0; k < 10; ++k) {
+        raw_m[k] = __ldg(mrow + k);
+        m[k] = mission_value(raw_m[k]);
+    }
+    tactical(raw_o, raw_m, tactical_out + sample * 24);
+    prior(o, m, st, prior_out + sample * 15);
+}
+
 constexpr int kMaxDevices = 64;
-constexpr size_t kDynSmem = sizeof(WarpSlot) * kWarps + sizeof(ChunkState); /* about 211 KiB */
+constexpr size_t kDynSmem = sizeof(WarpSlot) * kWarps + sizeof(ChunkState); /* about 199 KiB */
 int g_sms[kMaxDevices];
 
 } /* namespace */
@@ -985,16 +1029,21 @@ extern "C" int tb_cuda_extract_onboard_device(const float *device_obs, const flo
     if (!g_sms[dev]) {
         int sms = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-        if (cudaFuncSetAttribute(onboard_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(onboard_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kDynSmem)) != cudaSuccess)
             return 0;
         g_sms[dev] = sms;
     }
-    cudaGetLastError(); /* report this launch only */
-    /* one CTA per SM (shared memory admits one) */
+    cudaGetLastError(); /* report these launches only */
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    /* scans: one CTA per SM (shared memory admits one) */
     unsigned long long grid = static_cast<unsigned long long>(g_sms[dev]);
     if (grid > batch_size) grid = batch_size;
-    onboard_kernel<<<static_cast<unsigned int>(grid), kThreads, kDynSmem, static_cast<cudaStream_t>(stream)>>>(
+    onboard_scan_kernel<<<static_cast<unsigned int>(grid), kThreads, kDynSmem, s>>>(device_obs, device_mission,
+                                                                                  device_prior_15, batch_size);
+    /* control law: one thread per aircraft */
+    const unsigned long long control_grid = (batch_size + kControlThreads - 1) / kControlThreads;
+    onboard_control_kernel<<<static_cast<unsigned int>(control_grid), kControlThreads, 0, s>>>(
         device_obs, device_mission, device_tactical_24, device_prior_15, batch_size);
     return cudaGetLastError() == cudaSuccess;
 }
