@@ -546,7 +546,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                  "bytes_per_sample": bpa,
                  "roofline": {"bound": "hbm (78 % writes)", "achieved": a_ach, "peak": peak_gbs, "unit": "GB/s",
                               "frac": a_ach / peak_gbs, "peak_source": f"{peak_kind} hbm_gbs (copy)"},
-                 "launches": 2 * a_steps}
+                 "launches": 3 * a_steps}  # onboard scan + control, then the streaming kernel
         del a_outs
         torch.cuda.empty_cache()
 
@@ -565,7 +565,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                           "achieved_gbs": count * bpa / per_launch / 1e9}
         onboard = {"entry_point": "tb_cuda_extract_onboard_device", "outputs": "24 tactical + 15 prior",
                    "bound": "SM instruction issue (control law + LiDAR scans), not HBM", **legs,
-                   "launches": 2 * args.steps}
+                   "launches": 4 * args.steps}  # 2 mission sets x (scan + control kernels)
 
     # ---- simulator sensor rendering (tb_cuda_render_sensors_device), its own scenes
     sensors = None
