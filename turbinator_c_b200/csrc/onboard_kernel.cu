@@ -19,8 +19,8 @@
  *    the ballot, so the float sum keeps the reference's ray order and
  *    rounding.
  *  - Only aircraft whose mission reads the scans (dodge, slalom) are
- *    scanned; a CTA lists them per chunk of 512 aircraft and deals them to
- *    its warps round-robin (onboard_scan_kernel, one CTA per SM for its
+ *    scanned; a CTA lists them per chunk of 512 aircraft and its warps
+ *    claim them from a shared counter (onboard_scan_kernel, one CTA per SM for its
  *    shared-memory staging).  The scalar control law runs in a second launch,
  *    one aircraft per thread without shared memory (onboard_control_kernel),
  *    so a 65,536-aircraft batch is one wave; a scanned aircraft's results
@@ -837,15 +837,15 @@ __device__ void prior(const float *o, const float *m, const RayStats &rs, float 
  * each CTA owns a balanced contiguous range of aircraft and walks it kChunk
  * at a time; the aircraft whose mission reads the LiDAR scans (dodge:
  * nearest return; slalom: corridor) are listed in shared memory and the
- * warps take those scan jobs round-robin, each staging the next job's LiDAR
- * block with bulk copies while it scans the current one.  A scanned
+ * warps claim those scan jobs from a shared counter, each staging the next
+ * job's LiDAR block with bulk copies while it scans the current one.  A scanned
  * aircraft's RayStats go to the first six floats of its own prior row, which
  * the second launch reads back before overwriting the row.  (2)
  * onboard_control_kernel runs the control law, one aircraft per thread, with
  * no shared memory, so every aircraft of a 65,536 batch is in one wave. */
 struct ChunkState {
     unsigned short jobs[kChunk];   /* aircraft index in chunk | 0x4000 near | 0x8000 corridor */
-    int job_count;
+    int job_count, next_job;
 };
 
 /* The missions that read the scans (onboard_features.cuh:201-239). */
@@ -908,7 +908,10 @@ __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__r
 
     for (unsigned long long first = begin; first < end; first += kChunk) {
         const int n = static_cast<int>(end - first < kChunk ? end - first : kChunk);
-        if (threadIdx.x == 0) chunk.job_count = 0;
+        if (threadIdx.x == 0) {
+            chunk.job_count = 0;
+            chunk.next_job = 0;
+        }
         __syncthreads();
         /* (1) scan jobs of this chunk */
         for (int i = threadIdx.x; i < n; i += kThreads) {
@@ -919,18 +922,26 @@ __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__r
                     static_cast<unsigned short>(i | (dodge ? 0x4000 : 0) | (slalom ? 0x8000 : 0));
         }
         __syncthreads();
-        /* (2) scan jobs, round-robin over warps */
+        /* (2) scan jobs claimed from a shared counter, so a warp that drew
+         * short scans takes more; each warp stages the next job it claimed
+         * while it scans the current one (at most two staged at a time). */
         const int jobs = chunk.job_count;
-        int j = warp;
-        if (!failed && j < jobs)
-            stage_rays(slot, seq & 1, obs + (first + (chunk.jobs[j] & 0x3fff)) * kObsDim, bulk, lane);
-        for (; !failed && j < jobs; j += kWarps) {
-            const int job = chunk.jobs[j];
-            const int i = job & 0x3fff;
-            const bool more = j + kWarps < jobs;
+        int cur = jobs;
+        if (!failed) {
+            if (lane == 0) cur = atomicAdd(&chunk.next_job, 1);
+            cur = __shfl_sync(kFull, cur, 0);
+            if (cur < jobs)
+                stage_rays(slot, seq & 1, obs + (first + (chunk.jobs[cur] & 0x3fff)) * kObsDim, bulk, lane);
+        }
+        while (cur < jobs) {
+            int nxt = 0;
+            if (lane == 0) nxt = atomicAdd(&chunk.next_job, 1);
+            nxt = __shfl_sync(kFull, nxt, 0);
+            const bool more = nxt < jobs;
             if (more)
-                stage_rays(slot, (seq + 1) & 1, obs + (first + (chunk.jobs[j + kWarps] & 0x3fff)) * kObsDim,
-                           bulk, lane);
+                stage_rays(slot, (seq + 1) & 1, obs + (first + (chunk.jobs[nxt] & 0x3fff)) * kObsDim, bulk, lane);
+            const int job = chunk.jobs[cur];
+            const int i = job & 0x3fff;
             /* all lanes take the same branch, even if the copy lands at the deadline */
             if (!__all_sync(kFull, mbar_wait(smem_addr(&slot.bar[seq & 1]), (seq >> 1) & 1))) {
                 if (lane == 0) atomicOr(&g_onboard_status, 1u);
@@ -946,6 +957,7 @@ __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__r
                                           cos_az, sin_az, lane, (job & 0x4000) != 0, (job & 0x8000) != 0);
             if (lane == 0) park_stats(prior_out + (first + i) * 15, st);
             ++seq;
+            cur = nxt;
         }
         __syncthreads(); /* the job list is rewritten by the next chunk */
     }
