@@ -83,3 +83,30 @@ def bits_equal(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     a = np.ascontiguousarray(a, np.float32)
     b = np.ascontiguousarray(b, np.float32)
     return (a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))
+
+
+def random_scenes(seed: int, n: int, scenario=None, unit_attitude=True, obstacles=None, balls=None):
+    """Adversarial scenes for the culling and intersection code: random
+    attitudes (unit or not), spheres at random directions and distances
+    around the aircraft (some enclosing or grazing the sensors), random sky
+    distance and dome, any scenario."""
+    rng = np.random.default_rng(seed)
+    s = np.zeros(n, SCENE_DTYPE)
+    s["scenario"] = rng.integers(0, 28, n) if scenario is None else scenario
+    s["position"] = rng.uniform([-30, -30, -2], [30, 30, 20], (n, 3))
+    q = rng.normal(size=(n, 4))
+    s["attitude"] = q / np.linalg.norm(q, axis=1, keepdims=True) if unit_attitude else q
+    s["opponent"] = s["position"] + rng.normal(scale=3.0, size=(n, 3))
+    s["lidar_max"] = rng.choice([5.0, 30.0, 150.0], n)
+    s["dome_radius"] = rng.choice([10.0, 40.0, 400.0], n)
+    s["rng"] = rng.integers(0, 2**63, n, dtype=np.int64).astype(np.uint64)
+    s["step_index"] = rng.integers(-10, 100000, n)
+    s["player"] = rng.integers(0, 2, n)
+    s["sensors"] = 3
+    centres = s["position"][:, None, :] + rng.normal(scale=4.0, size=(n, MAX_OBSTACLES, 3))
+    radii = rng.uniform(0.0, 3.0, (n, MAX_OBSTACLES, 1))
+    s["obstacles"] = np.concatenate([centres, radii], axis=2)
+    s["obstacle_count"] = rng.integers(0, MAX_OBSTACLES + 1, n) if obstacles is None else obstacles
+    s["balls"] = s["position"][:, None, :] + rng.normal(scale=6.0, size=(n, MAX_BALLS, 3))
+    s["ball_count"] = rng.integers(0, MAX_BALLS + 1, n) if balls is None else balls
+    return s

@@ -20,7 +20,7 @@ import numpy as np
 import pytest
 
 import oracle
-from tests.sensor_cases import bits_equal, edge_scenes
+from tests.sensor_cases import bits_equal, edge_scenes, random_scenes
 from turbinator_c_b200.sensors import SCENE_DTYPE, synthetic_scenes, tb_cuda_render_sensors_device
 
 torch = pytest.importorskip("torch")
@@ -84,6 +84,18 @@ def test_synthetic_scenes_match_reference(kind):
 def test_edge_cases_match_reference():
     scenes = edge_scenes()
     assert_same(render_gpu(scenes, raw=True), oracle.render_sensors_reference(scenes, raw=True), "edge")
+
+
+@needs_reference
+@pytest.mark.parametrize("unit", [True, False])
+def test_adversarial_random_scenes_match_reference(unit):
+    """Spheres at random directions and distances around the sensors (some
+    enclosing them, some grazing the units' cones), random attitudes, any
+    scenario, sky distance and dome: the cases the exact culling must get
+    right.  Non-unit attitudes turn culling off and exercise the full path."""
+    scenes = random_scenes(1234 + unit, 2048, unit_attitude=unit)
+    want = oracle.render_sensors_reference(scenes)
+    assert_same(render_gpu(scenes), (want[0], want[1], want[2], None), f"random unit={unit}")
 
 
 @needs_reference

@@ -28,8 +28,9 @@
  *    hit" for every ray.  Either way the sphere is left out of that unit's
  *    list; the remaining spheres keep their order.  Only unit attitudes
  *    (|q|^2 within 1e-9 of 1) with finite geometry are culled; anything else
- *    keeps every sphere.  Likewise the arena dome is skipped for a unit whose
- *    origin is so far inside it that every dome hit lies beyond the sky.
+ *    keeps every sphere.  Likewise the arena dome is skipped (unit attitudes
+ *    only) for a unit whose origin is so far inside it that every dome hit
+ *    lies beyond the sky.
  *  - Body-frame ray directions do not depend on the scene: they are built on
  *    the host with the C library the simulator uses (sensor_rays.c) and read
  *    from global memory (SoA, coalesced); the kernel only rotates them.
@@ -289,9 +290,10 @@ __device__ __forceinline__ void unit_head(UnitHead &h, const tb_sensor_scene *__
     const double dome = bwb ? 300.0 : scene->dome_radius;
     h.dome_cc = ox * ox + oy * oy - dome * dome;
     /* Inside the cylinder at horizontal radius rho, a dome hit needs a
-     * horizontal run of at least dome - rho, so t >= dome - rho. */
+     * horizontal run of at least dome - rho, so t >= dome - rho for rays of
+     * unit length -- only when the attitude is a rotation (h.cull). */
     const double rho = sqrt(ox * ox + oy * oy);
-    h.dome = !(TB_SENSOR_CULL && dome - rho > h.best0 * (1 + 1e-9) + 1e-9);
+    h.dome = !(h.cull && dome - rho > h.best0 * (1 + 1e-9) + 1e-9);
     h.shelf = scenario == 10;
     h.arena = arena;
     h.n_obstacles = min(max(scene->obstacle_count, 0), TB_SENSOR_MAX_OBSTACLES);
