@@ -20,7 +20,17 @@
  *
  *   trainer_pattern <device> <batch> <steps> <seed> [dump_path [dump_batches]]
  *
- * Prints one summary line; exit status 0 iff every call succeeded and every
+ * With TB_PATTERN_BATCHED=1 in the environment the same observations go
+ * through fewer calls: after each simulator step (and any resets), the next
+ * observations, the post-reset observations and the next step's opponent
+ * observations -- all taken from the same simulator state the reference
+ * extracts them from -- are written by the simulator straight into
+ * consecutive rows of one buffer and extracted in one call of up to
+ * 3 x batch rows; TB_PATTERN_PINNED=1 in addition makes that buffer
+ * page-locked (cudaHostAlloc), as a trainer would allocate it.
+ *
+ * Prints one summary line (with the wall time spent in extraction calls,
+ * batching copies included); exit status 0 iff every call succeeded and every
  * sample matched.  With dump_path, the first dump_batches extracted batches
  * are written as records {int32 count; f32 obs[count*4148];
  * f32 mission[count*10]; u8 cameras[count*16384]}.
@@ -31,6 +41,9 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
+
+#include <cuda_runtime_api.h>
 
 #include "turbinator/c_api.h"
 #include "turbinator/training/cuda_features.h"
@@ -40,7 +53,7 @@ enum { OBS = 4148, MIS = 10, CAM = 16384, FEAT = 142, PRIV = 64, ACT = 15, SCENA
 
 typedef struct {
     long calls, samples, exact_mismatches, lidar_over, failures, arena_calls, resets;
-    double max_lidar_err;
+    double max_lidar_err, extract_ms;
     FILE *dump;
     int dump_left;
 } tally;
@@ -67,10 +80,19 @@ static void compare_batch(tally *t, const float *obs, const float *mission, cons
     t->samples += count;
 }
 
+static double now_ms(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1e3 + ts.tv_nsec * 1e-6;
+}
+
 static void extract_and_check(tally *t, tb_cuda_feature_batch *h, const float *obs, const float *mission,
                               const uint8_t *cams, float *features, int count) {
     ++t->calls;
-    if (!tb_cuda_extract_features_host(h, obs, mission, cams, (size_t)count, features)) {
+    const double t0 = now_ms();
+    const int ok = tb_cuda_extract_features_host(h, obs, mission, cams, (size_t)count, features);
+    t->extract_ms += now_ms() - t0;
+    if (!ok) {
         fprintf(stderr, "extraction failed: %s\n", tb_cuda_feature_batch_error(h));
         ++t->failures;
         return;
@@ -84,6 +106,27 @@ static void extract_and_check(tally *t, tb_cuda_feature_batch *h, const float *o
         fwrite(cams, 1, (size_t)count * CAM, t->dump);
         --t->dump_left;
     }
+}
+
+/* The rows of one batched call. */
+typedef struct {
+    float *obs, *mission, *features;
+    uint8_t *cams;
+    int count;
+} group;
+
+/* The next free rows of the batched call: observations are written straight
+ * into them by the simulator, so nothing is copied to batch. */
+static void group_slot(group *g, int count, float **obs, float **mission, uint8_t **cams) {
+    *obs = g->obs + (size_t)g->count * OBS;
+    *mission = g->mission + (size_t)g->count * MIS;
+    *cams = g->cams + (size_t)g->count * CAM;
+    g->count += count;
+}
+
+static void group_flush(tally *t, tb_cuda_feature_batch *h, group *g) {
+    if (g->count) extract_and_check(t, h, g->obs, g->mission, g->cams, g->features, g->count);
+    g->count = 0;
 }
 
 int main(int argc, char **argv) {
@@ -119,11 +162,30 @@ int main(int argc, char **argv) {
         !scenario)
         return 3;
 
+    const char *batched_env = getenv("TB_PATTERN_BATCHED");
+    const int batched = batched_env && atoi(batched_env) != 0;
     void *sim = tb_create(batch, seed);
-    tb_cuda_feature_batch *h = tb_cuda_feature_batch_create(device, B);
+    tb_cuda_feature_batch *h = tb_cuda_feature_batch_create(device, batched ? 3 * B : B);
     if (!sim || !h) {
         fprintf(stderr, "setup failed: %s\n", sim ? "feature handle" : tb_last_error());
         return 3;
+    }
+    /* batched mode: one call per step over the rows gathered here */
+    group g = {0};
+    const char *pinned_env = getenv("TB_PATTERN_PINNED");
+    const int pinned = batched && pinned_env && atoi(pinned_env) != 0;
+    if (batched && !pinned) {
+        g.obs = calloc(3 * B * OBS, sizeof(float));
+        g.mission = calloc(3 * B * MIS, sizeof(float));
+        g.cams = calloc(3 * B * CAM, 1);
+        g.features = calloc(3 * B * FEAT, sizeof(float));
+        if (!g.obs || !g.mission || !g.cams || !g.features) return 3;
+    } else if (pinned) { /* page-locked: the host ABI streams them at PCIe speed */
+        if (cudaHostAlloc((void **)&g.obs, 3 * B * OBS * sizeof(float), cudaHostAllocPortable) != cudaSuccess ||
+            cudaHostAlloc((void **)&g.mission, 3 * B * MIS * sizeof(float), cudaHostAllocPortable) != cudaSuccess ||
+            cudaHostAlloc((void **)&g.cams, 3 * B * CAM, cudaHostAllocPortable) != cudaSuccess ||
+            cudaHostAlloc((void **)&g.features, 3 * B * FEAT * sizeof(float), cudaHostAllocPortable) != cudaSuccess)
+            return 3;
     }
     int any_arena = 0;
     for (int i = 0; i < batch; ++i) {
@@ -131,21 +193,42 @@ int main(int argc, char **argv) {
         any_arena |= is_arena_scenario(scenario[i]);
         if (tb_reset_one(sim, i, scenario[i], seed + (uint64_t)i)) return 3;
     }
-    if (tb_observe_training_batch(sim, obs, mission, cams, priv, NULL)) return 3;
-    extract_and_check(&t, h, obs, mission, cams, features, batch);
+    if (!batched) {
+        if (tb_observe_training_batch(sim, obs, mission, cams, priv, NULL)) return 3;
+        extract_and_check(&t, h, obs, mission, cams, features, batch);
+    } else {
+        float *o, *m;
+        uint8_t *c;
+        group_slot(&g, batch, &o, &m, &c);
+        if (tb_observe_training_batch(sim, o, m, c, priv, NULL)) return 3;
+        if (any_arena && steps > 0) { /* the first step's opponents, same state */
+            group_slot(&g, batch, &o, &m, &c);
+            if (tb_observe_opponents_training_batch(sim, o, m, c)) return 3;
+            ++t.arena_calls;
+        }
+        group_flush(&t, h, &g);
+    }
 
     uint64_t resets = 0;
     for (int step = 0; step < steps; ++step) {
-        if (tb_reference_action_batch(sim, actions) ||
-            tb_observe_opponents_training_batch(sim, opp_obs, opp_mission, opp_cams))
-            return 3;
-        if (any_arena) {
-            ++t.arena_calls;
-            extract_and_check(&t, h, opp_obs, opp_mission, opp_cams, features, batch);
+        if (tb_reference_action_batch(sim, actions)) return 3;
+        if (!batched) {
+            if (tb_observe_opponents_training_batch(sim, opp_obs, opp_mission, opp_cams)) return 3;
+            if (any_arena) {
+                ++t.arena_calls;
+                extract_and_check(&t, h, opp_obs, opp_mission, opp_cams, features, batch);
+            }
         }
         if (tb_step(sim, actions, next_obs, rewards, terminated, truncated)) return 3;
-        if (tb_observe_training_batch(sim, next_obs, next_mission, next_cams, next_priv, NULL)) return 3;
-        extract_and_check(&t, h, next_obs, next_mission, next_cams, features, batch);
+        if (!batched) {
+            if (tb_observe_training_batch(sim, next_obs, next_mission, next_cams, next_priv, NULL)) return 3;
+            extract_and_check(&t, h, next_obs, next_mission, next_cams, features, batch);
+        } else {
+            float *o, *m;
+            uint8_t *c;
+            group_slot(&g, batch, &o, &m, &c);
+            if (tb_observe_training_batch(sim, o, m, c, next_priv, NULL)) return 3;
+        }
         int any_done = 0;
         for (int i = 0; i < batch; ++i) {
             if (!(terminated[i] || truncated[i])) continue;
@@ -160,18 +243,48 @@ int main(int argc, char **argv) {
             f = priv; priv = next_priv; next_priv = f;
             uint8_t *c = cams; cams = next_cams; next_cams = c;
         } else {
-            if (tb_observe_training_batch(sim, obs, mission, cams, priv, NULL)) return 3;
-            extract_and_check(&t, h, obs, mission, cams, features, batch);
+            if (!batched) {
+                if (tb_observe_training_batch(sim, obs, mission, cams, priv, NULL)) return 3;
+                extract_and_check(&t, h, obs, mission, cams, features, batch);
+            } else {
+                float *o, *m;
+                uint8_t *c;
+                group_slot(&g, batch, &o, &m, &c);
+                if (tb_observe_training_batch(sim, o, m, c, priv, NULL)) return 3;
+            }
             any_arena = 0;
             for (int i = 0; i < batch; ++i) any_arena |= is_arena_scenario(scenario[i]);
         }
+        if (batched) {
+            /* the next step's opponents come from this (post-reset) state,
+             * which the reference reads at the top of the next step */
+            if (any_arena && step + 1 < steps) {
+                float *o, *m;
+                uint8_t *c;
+                group_slot(&g, batch, &o, &m, &c);
+                if (tb_observe_opponents_training_batch(sim, o, m, c)) return 3;
+                ++t.arena_calls;
+            }
+            group_flush(&t, h, &g);
+        }
+    }
+    if (pinned) {
+        cudaFreeHost(g.obs);
+        cudaFreeHost(g.mission);
+        cudaFreeHost(g.cams);
+        cudaFreeHost(g.features);
+    } else {
+        free(g.obs);
+        free(g.mission);
+        free(g.cams);
+        free(g.features);
     }
     tb_cuda_feature_batch_destroy(h);
     tb_destroy(sim);
     if (t.dump) fclose(t.dump);
     printf("trainer-pattern: calls=%ld samples=%ld failures=%ld exact_mismatches=%ld lidar_over_tol=%ld "
-           "max_lidar_abs_err=%.3g arena_calls=%ld resets=%ld\n",
+           "max_lidar_abs_err=%.3g arena_calls=%ld resets=%ld extract_ms=%.3f batched=%d pinned=%d\n",
            t.calls, t.samples, t.failures, t.exact_mismatches, t.lidar_over, t.max_lidar_err, t.arena_calls,
-           t.resets);
+           t.resets, t.extract_ms, batched, pinned);
     return (t.failures || t.exact_mismatches || t.lidar_over) ? 1 : 0;
 }
