@@ -188,3 +188,22 @@ def test_cluster_sign_near_cancellation():
     obs[:, 48:4144] = lidar.reshape(n, 4096)
     out = run_onboard(obs, mission)
     check_onboard(out, obs, mission, "cluster-sign")
+
+
+def test_bounded_staging_wait_reports_and_recovers():
+    """A scanning aircraft whose LiDAR copy is withheld makes the scan
+    kernel's bounded wait expire: tb_cuda_synchronize reports it once, and the
+    next call is whole and correct."""
+    n = 64
+    obs, mission, _, _ = tb.generate(45, 0, n)
+    mission = mission.copy()
+    mission[:, 5] = 1.0  # every aircraft on a dodge mission: all are scan jobs
+    d_obs = torch.from_numpy(obs).cuda()
+    d_mis = torch.from_numpy(mission).cuda()
+    tac = torch.zeros((n, 24), device="cuda")
+    pri = torch.zeros((n, 15), device="cuda")
+    assert tb.tb_cuda_synchronize(None) == 1
+    assert tb.launch_onboard(d_obs, d_mis, tac, pri, n, None, wait_ns=20_000_000, stall_sample=5) == 1
+    assert tb.tb_cuda_synchronize(None) == 0
+    assert tb.tb_cuda_synchronize(None) == 1          # reported once, then cleared
+    check_onboard(run_onboard(obs, mission), obs, mission, "after-timeout")

@@ -89,6 +89,7 @@ def load_library() -> ctypes.CDLL:
     _bind(lib, "tb_cuda_render_sensors_device", _c.c_int, [_vp, _sz, _vp, _sz, _vp, _sz, _vp, _vp, _vp])
     _bind(lib, "tb_cuda_extract_features_device_sharded", _c.c_int,
           [_c.c_int, _c.POINTER(_c.c_int)] + [_c.POINTER(_vp)] * 4 + [_c.POINTER(_sz), _c.POINTER(_vp)])
+    _bind(lib, "tb_onboard_launch", _c.c_int, [_vp] * 4 + [_sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_actor_inputs_launch", _c.c_int, [_vp] * 9 + [_sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_launch_f32cam", _c.c_int,
           [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
@@ -220,6 +221,14 @@ def launch(obs, mission, cameras, features, batch_size: int, stream=None, *,
     return load_library().tb_features_launch(
         _ptr(obs), _ptr(mission), _ptr(cameras), _ptr(features), batch_size,
         _stream_handle(stream), _c.byref(opts))
+
+
+def launch_onboard(obs, mission, tactical, prior, batch_size: int, stream=None, *, wait_ns: int = 0,
+                   stall_sample: int = -1) -> int:
+    """tb_cuda_extract_onboard_device with the test hook (bounded waits)."""
+    opts = LaunchOpts(0, 0, wait_ns, stall_sample)
+    return load_library().tb_onboard_launch(_ptr(obs), _ptr(mission), _ptr(tactical), _ptr(prior), batch_size,
+                                            _stream_handle(stream), _c.byref(opts))
 
 
 def launch_actor_inputs(obs, mission, cameras, tactical, prior, proprio, mission_vec, lidar, luma, batch_size: int,

@@ -189,7 +189,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 /* Bounded wait (about one second of %globaltimer); false on expiry. */
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     unsigned long long t0, t1;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
@@ -197,7 +197,7 @@ __device__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(bar, parity)) return true;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-        if (t1 - t0 > kWaitNs) return false;
+        if (t1 - t0 > limit_ns) return false;
     }
 }
 
@@ -880,7 +880,9 @@ __device__ __forceinline__ RayStats unpark_stats(const float *row) {
 __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__restrict__ obs,
                                                                 const float *__restrict__ mission,
                                                                 float *__restrict__ prior_out,
-                                                                unsigned long long batch) {
+                                                                unsigned long long batch,
+                                                                unsigned long long wait_ns,
+                                                                long long stall_sample) {
     __shared__ RayTables tables;
     extern __shared__ __align__(128) unsigned char dyn[];
     build_ray_tables(tables);
@@ -930,23 +932,26 @@ __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__r
         if (!failed) {
             if (lane == 0) cur = atomicAdd(&chunk.next_job, 1);
             cur = __shfl_sync(kFull, cur, 0);
-            if (cur < jobs)
-                stage_rays(slot, seq & 1, obs + (first + (chunk.jobs[cur] & 0x3fff)) * kObsDim, bulk, lane);
+            if (cur < jobs) {
+                const unsigned long long a = first + (chunk.jobs[cur] & 0x3fff);
+                if (static_cast<long long>(a) != stall_sample) /* test hook: withhold a copy */
+                    stage_rays(slot, seq & 1, obs + a * kObsDim, bulk, lane);
+            }
         }
         while (cur < jobs) {
             int nxt = 0;
             if (lane == 0) nxt = atomicAdd(&chunk.next_job, 1);
             nxt = __shfl_sync(kFull, nxt, 0);
             const bool more = nxt < jobs;
-            if (more)
+            if (more && static_cast<long long>(first + (chunk.jobs[nxt] & 0x3fff)) != stall_sample)
                 stage_rays(slot, (seq + 1) & 1, obs + (first + (chunk.jobs[nxt] & 0x3fff)) * kObsDim, bulk, lane);
             const int job = chunk.jobs[cur];
             const int i = job & 0x3fff;
             /* all lanes take the same branch, even if the copy lands at the deadline */
-            if (!__all_sync(kFull, mbar_wait(smem_addr(&slot.bar[seq & 1]), (seq >> 1) & 1))) {
+            if (!__all_sync(kFull, mbar_wait(smem_addr(&slot.bar[seq & 1]), (seq >> 1) & 1, wait_ns))) {
                 if (lane == 0) atomicOr(&g_onboard_status, 1u);
                 /* no copy may still be in flight into this warp's shared memory */
-                if (more) mbar_wait(smem_addr(&slot.bar[(seq + 1) & 1]), ((seq + 1) >> 1) & 1);
+                if (more) mbar_wait(smem_addr(&slot.bar[(seq + 1) & 1]), ((seq + 1) >> 1) & 1, wait_ns);
                 failed = true;
                 break;
             }
@@ -1025,9 +1030,12 @@ extern "C" int tb_onboard_status_take(void *stream, unsigned int *status) {
     return 1;
 }
 
-extern "C" int tb_cuda_extract_onboard_device(const float *device_obs, const float *device_mission,
-                                              float *device_tactical_24, float *device_prior_15,
-                                              size_t batch_size, void *stream) {
+/* Both launches; opts may be NULL (its wait_ns and stall_sample fields are
+ * honoured: a test withholds one scanning aircraft's staging copy so the
+ * bounded wait expires). */
+extern "C" int tb_onboard_launch(const float *device_obs, const float *device_mission, float *device_tactical_24,
+                                 float *device_prior_15, size_t batch_size, void *stream,
+                                 const tb_features_launch_opts *opts) {
     if (!device_obs || !device_mission || !device_tactical_24 || !device_prior_15 || batch_size == 0 ||
         batch_size > 0x7fffffffu)
         return 0;
@@ -1046,16 +1054,25 @@ extern "C" int tb_cuda_extract_onboard_device(const float *device_obs, const flo
             return 0;
         g_sms[dev] = sms;
     }
+    const unsigned long long wait_ns = (opts && opts->wait_ns) ? opts->wait_ns : kWaitNs;
+    const long long stall_sample = opts ? opts->stall_sample : -1;
     cudaGetLastError(); /* report these launches only */
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     /* scans: one CTA per SM (shared memory admits one) */
     unsigned long long grid = static_cast<unsigned long long>(g_sms[dev]);
     if (grid > batch_size) grid = batch_size;
-    onboard_scan_kernel<<<static_cast<unsigned int>(grid), kThreads, kDynSmem, s>>>(device_obs, device_mission,
-                                                                                  device_prior_15, batch_size);
+    onboard_scan_kernel<<<static_cast<unsigned int>(grid), kThreads, kDynSmem, s>>>(
+        device_obs, device_mission, device_prior_15, batch_size, wait_ns, stall_sample);
     /* control law: one thread per aircraft */
     const unsigned long long control_grid = (batch_size + kControlThreads - 1) / kControlThreads;
     onboard_control_kernel<<<static_cast<unsigned int>(control_grid), kControlThreads, 0, s>>>(
         device_obs, device_mission, device_tactical_24, device_prior_15, batch_size);
     return cudaGetLastError() == cudaSuccess;
+}
+
+extern "C" int tb_cuda_extract_onboard_device(const float *device_obs, const float *device_mission,
+                                              float *device_tactical_24, float *device_prior_15,
+                                              size_t batch_size, void *stream) {
+    return tb_onboard_launch(device_obs, device_mission, device_tactical_24, device_prior_15, batch_size, stream,
+                             nullptr);
 }

@@ -60,6 +60,11 @@ int tb_features_status_enqueue(void *stream, unsigned int *host_word);
 /* Clear the current device's status word (synchronous on `stream`). */
 int tb_features_status_clear(void *stream);
 
+/* tb_cuda_extract_onboard_device with launch options (wait_ns and stall_sample
+ * are honoured); opts may be NULL. */
+int tb_onboard_launch(const float *obs, const float *mission, float *tactical, float *prior, size_t batch,
+                      void *stream, const tb_features_launch_opts *opts);
+
 /* As tb_features_status_take, for the onboard kernel's own status word. */
 int tb_onboard_status_take(void *stream, unsigned int *status);
 
