@@ -43,7 +43,9 @@
  * caller's buffers directly (faster at that size than staging on one
  * thread); larger ones are staged, one host thread per TB_STAGE_ROWS rows up
  * to the lane count. */
+#ifndef TB_STAGED_MIN_ROWS
 #define TB_STAGED_MIN_ROWS ((size_t)512)
+#endif
 
 #define TB_IN_ROW_BYTES (TB_OBS_DIM * sizeof(float) + TB_MISSION_DIM * sizeof(float) + TB_CAMERA_BYTES)
 #define TB_OUT_ROW_BYTES (TB_FEATURE_DIM * sizeof(float))
@@ -374,14 +376,16 @@ static void *job_main(void *arg) {
         job_run_direct(job);
     else
         job_run_staged(job);
-    /* read the kernels' status word behind this lane's work on each stream */
-    for (int b = 0; b < 2; ++b) {
-        job->lane->status[b] = 0;
+    /* read the kernels' status word behind this lane's work on each stream it
+     * used (a job of one chunk uses stream 0 only) */
+    const size_t chunk_rows = job->direct_in ? TB_DIRECT_CHUNK : job->lane->stage_rows;
+    const int used = job->count > chunk_rows ? 2 : 1;
+    job->lane->status[0] = job->lane->status[1] = 0;
+    for (int b = 0; b < used; ++b)
         if (!job->stage && !tb_features_status_enqueue(job->lane->streams[b], &job->lane->status[b]))
             job_fail(job, "synchronize features", cudaGetLastError());
-    }
     /* leave nothing in flight that reads or writes the caller's buffers */
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < used; ++b) {
         st = cudaStreamSynchronize(job->lane->streams[b]);
         if (st != cudaSuccess) job_fail(job, "synchronize features", st);
     }
