@@ -56,20 +56,33 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr unsigned long long kWaitNs = 1000000000ull; /* ~1 s limit on each staging wait */
 constexpr uint32_t kHeadBlockBytes = 6 * 128 * 4;      /* elevation rows 0..5 of one head */
 
-/* ---- correctly rounded float transcendentals (double, one rounding) ---- */
-__device__ __forceinline__ float cr_sin(float x) { return static_cast<float>(sin(static_cast<double>(x))); }
-__device__ __forceinline__ float cr_cos(float x) { return static_cast<float>(cos(static_cast<double>(x))); }
-__device__ __forceinline__ float cr_tan(float x) { return static_cast<float>(tan(static_cast<double>(x))); }
-__device__ __forceinline__ float cr_asin(float x) { return static_cast<float>(asin(static_cast<double>(x))); }
-__device__ __forceinline__ float cr_acos(float x) { return static_cast<float>(acos(static_cast<double>(x))); }
-__device__ __forceinline__ float cr_atanh(float x) { return static_cast<float>(atanh(static_cast<double>(x))); }
-__device__ __forceinline__ float cr_tanh(float x) { return static_cast<float>(tanh(static_cast<double>(x))); }
-__device__ __forceinline__ float cr_exp(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
+/* ---- correctly rounded float transcendentals (double, one rounding) ----
+ * One out-of-line copy of each double-precision function, shared by every
+ * call site: the control law calls them about 80 times, and inlined copies
+ * made its code too large for the instruction caches. */
+__device__ __noinline__ double d_sin(double x) { return sin(x); }
+__device__ __noinline__ double d_cos(double x) { return cos(x); }
+__device__ __noinline__ double d_tan(double x) { return tan(x); }
+__device__ __noinline__ double d_asin(double x) { return asin(x); }
+__device__ __noinline__ double d_acos(double x) { return acos(x); }
+__device__ __noinline__ double d_atanh(double x) { return atanh(x); }
+__device__ __noinline__ double d_tanh(double x) { return tanh(x); }
+__device__ __noinline__ double d_exp(double x) { return exp(x); }
+__device__ __noinline__ double d_atan2(double y, double x) { return atan2(y, x); }
+__device__ __noinline__ double d_hypot(double x, double y) { return hypot(x, y); }
+__device__ __forceinline__ float cr_sin(float x) { return static_cast<float>(d_sin(static_cast<double>(x))); }
+__device__ __forceinline__ float cr_cos(float x) { return static_cast<float>(d_cos(static_cast<double>(x))); }
+__device__ __forceinline__ float cr_tan(float x) { return static_cast<float>(d_tan(static_cast<double>(x))); }
+__device__ __forceinline__ float cr_asin(float x) { return static_cast<float>(d_asin(static_cast<double>(x))); }
+__device__ __forceinline__ float cr_acos(float x) { return static_cast<float>(d_acos(static_cast<double>(x))); }
+__device__ __forceinline__ float cr_atanh(float x) { return static_cast<float>(d_atanh(static_cast<double>(x))); }
+__device__ __forceinline__ float cr_tanh(float x) { return static_cast<float>(d_tanh(static_cast<double>(x))); }
+__device__ __forceinline__ float cr_exp(float x) { return static_cast<float>(d_exp(static_cast<double>(x))); }
 __device__ __forceinline__ float cr_atan2(float y, float x) {
-    return static_cast<float>(atan2(static_cast<double>(y), static_cast<double>(x)));
+    return static_cast<float>(d_atan2(static_cast<double>(y), static_cast<double>(x)));
 }
 __device__ __forceinline__ float cr_hypot(float x, float y) {
-    return static_cast<float>(hypot(static_cast<double>(x), static_cast<double>(y)));
+    return static_cast<float>(d_hypot(static_cast<double>(x), static_cast<double>(y)));
 }
 
 /* ---- the reference's small helpers (onboard_features.cuh:6-22) ---- */
@@ -970,7 +983,7 @@ __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__r
 
 constexpr int kControlThreads = 128;
 
-__global__ void __launch_bounds__(kControlThreads) onboard_control_kernel(const float *__restrict__ obs,
+__global__ void __launch_bounds__(kControlThreads, 4) onboard_control_kernel(const float *__restrict__ obs,
                                                                           const float *__restrict__ mission,
                                                                           float *__restrict__ tactical_out,
                                                                           float *__restrict__ prior_out,
