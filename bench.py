@@ -702,6 +702,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                                      "trainer passes them"}},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                     "peak_note": "the copy peak is a device copy (half writes, fixed grid); this kernel "
+                                  "reads 98 % of its bytes, and the best read-only stream measured on "
+                                  "this pool is 7,094 GB/s (profiles/hbm_patterns_b200.md)",
                      "traffic": (tps * count) if tps else None,
                      "algorithmic_bytes_per_launch": count * tb.BYTES_PER_SAMPLE,
                      "kernel": "features_staged_kernel", "avg_launch_ms": avg_launch_s * 1e3},

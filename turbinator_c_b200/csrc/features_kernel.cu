@@ -17,8 +17,13 @@
  *    per aircraft, ~1 flop per byte.  It is bound by HBM bandwidth, so the
  *    kernel is built to keep enough bytes in flight and to touch every byte
  *    exactly once.
- *  - Persistent CTAs (grid = SMs x resident CTAs) with one producer warp and
- *    eight consumer warps.  The producer streams each aircraft's
+ *  - CTAs of one producer warp and eight consumer warps.  With u8 cameras
+ *    each CTA takes a run of up to 8 consecutive aircraft (fewer when the
+ *    batch would not fill the resident CTAs) and the grid covers the batch,
+ *    so the hardware hands CTAs to SMs as they free up; a persistent
+ *    grid with a fixed share per CTA (kept for FP32 cameras, whose 1 CTA
+ *    per SM would drain its ring at every CTA change) ends when its slowest
+ *    SMs do, ~11 % later at 65,536 aircraft.  The producer streams each aircraft's
  *    observation row (16,592 B) and camera block (16,384 B) into a
  *    shared-memory ring with 1-D bulk copies (cp.async.bulk, completion
  *    counted in bytes on an mbarrier) and its 40-byte mission row with
@@ -68,8 +73,9 @@ constexpr uint32_t kBarrierRegion = 128;
 
 /* Shared-memory ring geometry per camera format.  A stage holds one
  * aircraft: observation row, camera block, mission row.  u8 cameras: 33 KB
- * stages, 3 per CTA, 2 CTAs per SM; FP32 cameras: 82 KB stages, 2 per CTA,
- * 1 CTA per SM.  Either way ~160-200 KB per SM are in flight. */
+ * stages, 3 per CTA, 2 CTAs per SM, runs of `chunk` aircraft per CTA; FP32
+ * cameras: 82 KB stages, 2 per CTA, 1 persistent CTA per SM.  Either way
+ * ~160-200 KB per SM are in flight. */
 template <bool kF32Cam>
 struct Ring {
     static constexpr uint32_t camera_bytes = kF32Cam ? 4u * kCameraBytes : kCameraBytes;
@@ -79,6 +85,7 @@ struct Ring {
     static constexpr int stages = kF32Cam ? 2 : 3;
     static constexpr int min_blocks = kF32Cam ? 1 : 2;
     static constexpr uint32_t smem_bytes = kBarrierRegion + stages * stage_bytes;
+    static constexpr unsigned long long max_chunk = kF32Cam ? 0 : 8; /* 0: persistent grid-stride */
 };
 static_assert(Ring<false>::stage_bytes == 33024 && Ring<true>::stage_bytes == 82176, "stage layout");
 
@@ -188,7 +195,8 @@ __device__ __forceinline__ float luma_bytes4(const float4 v) {
 }
 
 /* ------------------------------------------------------------------ */
-/* Staged kernel: persistent, warp-specialised, bulk-copy pipeline. */
+/* Staged kernel: warp-specialised bulk-copy pipeline over runs of aircraft
+ * (or a persistent grid-stride loop when a.chunk is 0). */
 
 struct StagedArgs {
     const float *obs;
@@ -196,6 +204,7 @@ struct StagedArgs {
     const void *cameras; /* u8 or f32 camera rows; may be NULL */
     float *features;
     unsigned long long batch;
+    unsigned long long chunk; /* > 0: CTA c takes aircraft [c*chunk, (c+1)*chunk); 0: grid-stride */
     unsigned long long wait_ns;
     long long stall_sample; /* test hook: >= 0 withholds that sample's copies */
 };
@@ -221,8 +230,12 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
     }
     __syncthreads();
 
-    const unsigned long long first = blockIdx.x;
-    const unsigned long long step = gridDim.x;
+    unsigned long long first = blockIdx.x, last = a.batch, step = gridDim.x;
+    if (a.chunk) {
+        first = static_cast<unsigned long long>(blockIdx.x) * a.chunk;
+        last = first + a.chunk < a.batch ? first + a.chunk : a.batch;
+        step = 1;
+    }
 
     if (warp == kConsumerWarps) {
         /* ---------------- producer warp ---------------- */
@@ -231,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
         const unsigned char *cameras = static_cast<const unsigned char *>(a.cameras);
         unsigned long long k = 0;
         bool ok = true;
-        for (unsigned long long sample = first; sample < a.batch; sample += step, ++k) {
+        for (unsigned long long sample = first; sample < last; sample += step, ++k) {
             const int s = static_cast<int>(k % R::stages);
             const uint32_t phase = static_cast<uint32_t>((k / R::stages) & 1);
             /* warp-uniform: every lane leaves together or none does */
@@ -273,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
     const int cam = warp >> 1;           /* camera half-image w */
     const int qy = warp & 1;
     unsigned long long k = 0;
-    for (unsigned long long sample = first; sample < a.batch; sample += step, ++k) {
+    for (unsigned long long sample = first; sample < last; sample += step, ++k) {
         const int s = static_cast<int>(k % R::stages);
         const uint32_t phase = static_cast<uint32_t>((k / R::stages) & 1);
         if (!__all_sync(0xffffffffu, mbar_wait(full_bar + 8 * s, phase, a.wait_ns))) {
@@ -508,9 +521,20 @@ static int launch_features(const float *obs, const float *mission, const void *c
         args.batch = batch;
         args.wait_ns = (opts && opts->wait_ns) ? opts->wait_ns : kDefaultWaitNs;
         args.stall_sample = opts ? opts->stall_sample : -1;
-        unsigned long long grid = static_cast<unsigned long long>(info->sms) *
-                                  static_cast<unsigned long long>(info->blocks_per_sm[kF32Cam ? 1 : 0]);
-        if (opts && opts->grid_limit > 0 && grid > static_cast<unsigned long long>(opts->grid_limit))
+        /* runs of Ring::chunk aircraft over a covering grid, or (FP32 cameras,
+         * and the ring-wraparound test hook `grid_limit`) a persistent grid */
+        const bool limited = opts && opts->grid_limit > 0;
+        const unsigned long long resident = static_cast<unsigned long long>(info->sms) *
+                                            static_cast<unsigned long long>(info->blocks_per_sm[kF32Cam ? 1 : 0]);
+        unsigned long long grid = resident;
+        args.chunk = 0;
+        if (!limited && Ring<kF32Cam>::max_chunk) {
+            /* runs of up to max_chunk aircraft, but no fewer CTAs than fit at once */
+            const unsigned long long fill = (batch + resident - 1) / resident;
+            args.chunk = fill < Ring<kF32Cam>::max_chunk ? fill : Ring<kF32Cam>::max_chunk;
+            grid = (batch + args.chunk - 1) / args.chunk;
+        }
+        if (limited && grid > static_cast<unsigned long long>(opts->grid_limit))
             grid = static_cast<unsigned long long>(opts->grid_limit);
         if (grid > batch) grid = batch;
         features_staged_kernel<kF32Cam>
