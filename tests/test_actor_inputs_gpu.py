@@ -90,7 +90,8 @@ def test_edge_values():
     check(obs, mission, cams, "edge")
 
 
-@pytest.mark.parametrize("n", [1, 3, 1185])
+# runs of 1 aircraft per CTA up to 296 aircraft, then runs of 2 (297 and 1,185 end in a run of 1)
+@pytest.mark.parametrize("n", [1, 3, 296, 297, 1185])
 def test_ragged_batches(n):
     obs, mission, cams, _ = tb.generate(42, 0, n)
     check(obs, mission, cams, f"B={n}")

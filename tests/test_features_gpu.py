@@ -101,7 +101,10 @@ def test_config4_stress_quarters_full_size():
     assert np.all(d == d[0, 0])                                                   # (d) identical
 
 
-@pytest.mark.parametrize("batch", [1, 2, 3, 7, 147, 148, 149, 295, 296, 297, 1023, 1025])
+# 296 CTAs are resident at once: batches past that go in runs of ceil(B / 296) aircraft per CTA
+# (at most 8), so 297, 593, 2,367, 2,369 and 9,001 end in a shorter run
+@pytest.mark.parametrize("batch", [1, 2, 3, 7, 147, 148, 149, 295, 296, 297, 592, 593, 1023, 1025,
+                                   2367, 2368, 2369, 9001])
 def test_ragged_batch_sizes(batch):
     obs, mission, cams, _ = tb.generate(21, 0, batch)
     check_features(run_device(obs, mission, cams), oracle.features(obs, mission, cams), f"B={batch}")
