@@ -39,6 +39,7 @@
  */
 #include <cuda_runtime.h>
 
+#include <stddef.h>
 #include <stdint.h>
 
 #include "tb_features_internal.h"
@@ -183,11 +184,17 @@ __device__ unsigned int g_onboard_status;
  * next copy, and the others cover the wait.  Two blocks per warp (a prefetch
  * ring, 18 KB a warp) fitted 11 warps: 0.137 / 0.362 ms against 0.115 /
  * 0.270 ms now per 65,536-aircraft call (mission mix / all scanning). */
-struct WarpSlot {
+struct alignas(16) WarpSlot {
     float ranges[kRays];
     float corridor_x[kRays];
     unsigned long long bar;
 };
+/* Bulk copies land at ranges and ranges + kRays / 2 of every warp's slot, and
+ * need 16-byte aligned shared addresses: the slots are packed back to back
+ * from a 128-byte aligned base, so the slot size must be a multiple of 16
+ * (12,296 bytes unpadded would leave odd warps' slots 8-byte aligned). */
+static_assert(sizeof(WarpSlot) % 16 == 0 && offsetof(WarpSlot, ranges) == 0 && (kRays / 2 * 4) % 16 == 0,
+              "bulk-copy destinations must be 16-byte aligned");
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
