@@ -176,17 +176,21 @@ __device__ __forceinline__ uint32_t byte_sum4(uint32_t w, uint32_t acc) {
  * the clamp of src/sim/sim_internal.h:73): fmax(0, fmin(255, round(v*255)))
  * in double, so NaN gives 255.  Evaluated exactly in float, as a float byte
  * value: NaN is tested explicitly (a fused clamp would send it to 0);
- * clamping other values to [0, 1] first gives the same byte; v*255 is formed
- * as hi + lo with lo the exact FMA residual, and round-half-away of hi is
- * taken one lower when hi landed on a half-integer from below (lo < 0).  No
- * other case can straddle a rounding boundary, because half-integers below
- * 256 are themselves floats. */
+ * clamping other values to [0, 1] first gives the same byte.  v*255 is formed
+ * as hi + lo with lo the exact FMA residual; hi is rounded to the nearest
+ * integer, ties to even, by adding and subtracting 2^23 (exact for
+ * 0 <= hi <= 255).  Only when hi is itself a half-integer can that differ from
+ * rounding the exact product half away from zero (half-integers below 256
+ * are floats, so no other rounding boundary lies between hi and hi + lo);
+ * there the byte is hi + 0.5 when lo >= 0 and hi - 0.5 when lo < 0 (an exact
+ * residual of zero is +0).  Checked against round-half-away of v*255 in
+ * double for every float in [0, 1]. */
 __device__ __forceinline__ float luma_byte(float v) {
     const float c = fmaxf(fminf(v, 1.0f), 0.0f);
     const float hi = __fmul_rn(c, 255.0f);
     const float lo = __fmaf_rn(c, 255.0f, -hi);
-    const float r = roundf(hi);
-    const float q = (r - hi == 0.5f && lo < 0.0f) ? r - 1.0f : r;
+    const float r = __fsub_rn(__fadd_rn(hi, 8388608.0f), 8388608.0f);
+    const float q = fabsf(__fsub_rn(r, hi)) == 0.5f ? __fadd_rn(hi, copysignf(0.5f, lo)) : r;
     return v != v ? 255.0f : q;
 }
 
