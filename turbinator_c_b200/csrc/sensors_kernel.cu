@@ -137,12 +137,22 @@ struct UnitScene {
 };
 
 /* sphere_hit (sensors.c:4-10) with the ray-independent terms precomputed in
- * the same rounding: b = oc.d, disc = (b*b - oc.oc) + r*r. */
-__device__ __forceinline__ double sphere_hit(const UnitScene &s, int i, Vec d) {
+ * the same rounding: b = oc.d, disc = (b*b - oc.oc) + r*r.  `best` is the
+ * caller's nearest hit so far: a sphere whose near intersection -b - sqrt(disc)
+ * lies beyond it cannot change the result, and is dropped without the square
+ * root when L = -b - best > 0 and L*L > disc by a relative 1e-9, with
+ * L > 1e-6 (|b| + best).  Then sqrt(disc) < L (1 - 5e-10), so -b - sqrt(disc)
+ * exceeds best by at least 5e-10 L > 4.4e-16 (|b| + best), more than the
+ * rounding of L, of the square root and of the subtraction together: the
+ * simulator's own arithmetic would have found t >= best (its far root is
+ * larger still) and kept best. */
+__device__ __forceinline__ double sphere_hit(const UnitScene &s, int i, Vec d, double best) {
     const double2 xy = s.oc_xy[i], zq = s.oc_zq[i];
     const double b = xy.x * d.x + xy.y * d.y + zq.x * d.z;
     const double disc = b * b - zq.y + s.rr[i];
     if (disc < 0) return INFINITY;
+    const double lead = -b - best;
+    if (lead > 1e-6 * (fabs(b) + best) && lead * lead > disc * (1 + 1e-9)) return INFINITY;
     const double root = sqrt(disc);
     double t = -b - root;
     if (t <= 0.05) t = -b + root;
@@ -172,7 +182,7 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
     }
     int i = 0;
     for (; i < s.kept_obstacles; ++i) {
-        const double t = sphere_hit(s, i, d);
+        const double t = sphere_hit(s, i, d, best);
         if (t < best) {
             best = t;
             kind = 1;
@@ -180,7 +190,7 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
     }
     if (s.h.arena) {
         if (s.kept_opponent) {
-            const double t = sphere_hit(s, i, d);
+            const double t = sphere_hit(s, i, d, best);
             if (t < best) {
                 best = t;
                 kind = 2;
@@ -200,7 +210,7 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
         }
     }
     for (; i < s.kept_total; ++i) {
-        const double t = sphere_hit(s, i, d);
+        const double t = sphere_hit(s, i, d, best);
         if (t < best) {
             best = t;
             kind = 4;
