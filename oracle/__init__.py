@@ -17,6 +17,8 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_PATH = os.path.join(HERE, "liboracle.so")
+# the renderer restatement with the product kernel's square-root skip (test build)
+ORACLE_SKIP_PATH = os.path.join(HERE, "liboracle_skip.so")
 REF_TRAINING_PATH = os.path.join(HERE, "_ref", "libtb_ref_training.so")
 REF_ONBOARD_PATH = os.path.join(HERE, "_ref", "libtb_ref_onboard.so")
 REF_ONBOARD_CR_PATH = os.path.join(HERE, "_ref", "libtb_ref_onboard_cr.so")
@@ -296,15 +298,39 @@ def _sensor_outputs(n: int, raw: bool):
     return lidar, valid, cams, raws
 
 
-def render_sensors_port(scenes, raw: bool = False):
+_oracle_skip = None
+
+
+def _sensor_port_skip() -> ctypes.CDLL:
+    global _oracle_skip
+    if _oracle_skip is None:
+        if not os.path.exists(ORACLE_SKIP_PATH):
+            raise RuntimeError(f"{ORACLE_SKIP_PATH} missing: run `make -C oracle`")
+        l = ctypes.CDLL(ORACLE_SKIP_PATH)
+        l.oracle_render_sensors.restype = None
+        l.oracle_render_sensors.argtypes = [_vp, ctypes.c_int64, _vp, ctypes.c_int64, _vp, ctypes.c_int64, _vp, _vp]
+        l.oracle_sqrt_skips.restype = ctypes.c_uint64
+        l.oracle_sqrt_skips.argtypes = []
+        _oracle_skip = l
+    return _oracle_skip
+
+
+def render_sensors_port(scenes, raw: bool = False, sqrt_skip: bool = False):
     """Restated renderers (sensors_oracle.c): (lidar [n,4096], valid [n,2],
-    cameras [n,16384], raw [n,147456] or None); unrendered rows keep NaN / 0."""
+    cameras [n,16384], raw [n,147456] or None); unrendered rows keep NaN / 0.
+    sqrt_skip=True renders with the test build that drops spheres without the
+    square root under the product kernel's condition."""
     scenes = np.ascontiguousarray(scenes)
     n = scenes.shape[0]
     lidar, valid, cams, raws = _sensor_outputs(n, raw)
-    _sensor_port().oracle_render_sensors(_addr(scenes), n, _addr(lidar), 4096, _addr(valid), 2, _addr(cams),
-                                         _addr(raws))
+    port = _sensor_port_skip() if sqrt_skip else _sensor_port()
+    port.oracle_render_sensors(_addr(scenes), n, _addr(lidar), 4096, _addr(valid), 2, _addr(cams), _addr(raws))
     return lidar, valid, cams, raws
+
+
+def sqrt_skips() -> int:
+    """Spheres the skip build has dropped so far in this process."""
+    return int(_sensor_port_skip().oracle_sqrt_skips())
 
 
 def render_sensors_reference(scenes, raw: bool = False, threads: int = 0):

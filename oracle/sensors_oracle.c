@@ -72,11 +72,33 @@ static int oarena(int scenario) {
     }
 }
 
-static double osphere(ovec origin, ovec dir, ovec centre, double radius) {
+/* Built with ORACLE_SQRT_SKIP (only into oracle/liboracle_skip.so, a test
+ * build), a sphere is dropped without the square root under the condition
+ * the product kernel uses (sphere_hit in sensors_kernel.cu): L = -along - best
+ * > 1e-6 (|along| + best) and L*L > disc (1 + 1e-9).  The test renders scenes
+ * with both builds and requires identical bits, i.e. that the condition only
+ * fires where this function's result could not have been nearer than best;
+ * oracle_sqrt_skips() counts the drops so the test can see that it fires.
+ * The default build is the simulator's arithmetic unchanged. */
+#ifdef ORACLE_SQRT_SKIP
+static uint64_t g_sqrt_skips;
+uint64_t oracle_sqrt_skips(void) { return g_sqrt_skips; }
+#endif
+
+static double osphere(ovec origin, ovec dir, ovec centre, double radius, double best) {
     ovec rel = ov(origin.x - centre.x, origin.y - centre.y, origin.z - centre.z);
     double along = odot(rel, dir);
     double disc = along * along - odot(rel, rel) + radius * radius;
     if (disc < 0) return INFINITY;
+#ifdef ORACLE_SQRT_SKIP
+    double lead = -along - best;
+    if (lead > 1e-6 * (fabs(along) + best) && lead * lead > disc * (1 + 1e-9)) {
+        ++g_sqrt_skips;
+        return INFINITY;
+    }
+#else
+    (void)best;
+#endif
     double root = sqrt(disc);
     double t = -along - root;
     if (t <= 0.05) t = -along + root;
@@ -102,11 +124,11 @@ static double ocast(const tb_sensor_scene *s, ovec o, ovec d, int *kind) {
     const int obstacles = oclamp_count(s->obstacle_count, TB_SENSOR_MAX_OBSTACLES);
     for (int i = 0; i < obstacles; i++) {
         const double *ob = s->obstacles[i];
-        double t = osphere(o, d, ov(ob[0], ob[1], ob[2]), ob[3]);
+        double t = osphere(o, d, ov(ob[0], ob[1], ob[2]), ob[3], nearest);
         if (t < nearest) { nearest = t; *kind = 1; }
     }
     if (oarena(s->scenario)) {
-        double t = osphere(o, d, ov(s->opponent[0], s->opponent[1], s->opponent[2]), bwb ? 0.75 : 0.45);
+        double t = osphere(o, d, ov(s->opponent[0], s->opponent[1], s->opponent[2]), bwb ? 0.75 : 0.45, nearest);
         if (t < nearest) { nearest = t; *kind = 2; }
         double dome = bwb ? 300 : s->dome_radius;
         double qa = d.x * d.x + d.y * d.y, qb = 2 * (o.x * d.x + o.y * d.y);
@@ -119,7 +141,7 @@ static double ocast(const tb_sensor_scene *s, ovec o, ovec d, int *kind) {
     }
     const int balls = oclamp_count(s->ball_count, TB_SENSOR_MAX_BALLS);
     for (int i = 0; i < balls; i++) {
-        double t = osphere(o, d, ov(s->balls[i][0], s->balls[i][1], s->balls[i][2]), 0.25);
+        double t = osphere(o, d, ov(s->balls[i][0], s->balls[i][1], s->balls[i][2]), 0.25, nearest);
         if (t < nearest) { nearest = t; *kind = 4; }
     }
     return nearest;

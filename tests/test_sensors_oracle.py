@@ -8,6 +8,8 @@
   restatement equals the reference renderers live on synthetic, heaviest-case,
   edge-case and simulated-episode scenes, and a scene packed from a simulated
   environment renders exactly as that environment does.
+* The product kernel's square-root skip (sphere_hit in sensors_kernel.cu),
+  built into a test copy of the restatement, changes no output bit.
 * The product's host-built body-frame ray tables (sensor_rays.c, compiled into
   libturbinator_cuda.so) equal the oracle's directions bit for bit, and
   tb_sensor_scene's numpy mirror matches the C layout.
@@ -22,7 +24,7 @@ import pytest
 
 import oracle
 import turbinator_c_b200 as tb
-from tests.sensor_cases import bits_equal, edge_scenes
+from tests.sensor_cases import bits_equal, edge_scenes, random_scenes
 from turbinator_c_b200.sensors import SCENE_DTYPE, synthetic_scenes
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "sensors_reference.npz")
@@ -102,3 +104,23 @@ def test_packed_scene_renders_as_its_environment():
     assert scenes["ball_count"].max() > 0
     _assert_same(oracle.render_sensors_reference(scenes), (lidar, valid, cams, None), "packed vs environment")
     _assert_same(oracle.render_sensors_port(scenes), (lidar, valid, cams, None), "port vs environment")
+
+
+@pytest.mark.parametrize("kind", ["flight", "max", "random", "edge"])
+def test_sqrt_skip_never_changes_a_render(kind):
+    """The product kernel drops a sphere without its square root when the
+    sphere's near intersection is provably beyond the ray's nearest hit so
+    far. The same condition, built into a copy of the restated renderer
+    (oracle/liboracle_skip.so), must leave every output bit unchanged; the
+    skip must also fire on the sphere-rich scenes, or the test proves nothing."""
+    if kind in ("flight", "max"):
+        scenes = synthetic_scenes(300 + len(kind), 64, balls=kind)
+    elif kind == "random":
+        scenes = np.concatenate([random_scenes(31, 48), random_scenes(32, 48, unit_attitude=False)])
+    else:
+        scenes = edge_scenes()
+    before = oracle.sqrt_skips()
+    _assert_same(oracle.render_sensors_port(scenes, raw=kind == "edge", sqrt_skip=True),
+                 oracle.render_sensors_port(scenes, raw=kind == "edge"), f"square-root skip/{kind}")
+    if kind in ("max", "random"):
+        assert oracle.sqrt_skips() > before, "the skip never fired"
