@@ -196,8 +196,13 @@ int tb_cuda_prepare_actor_inputs_device(const float *device_obs,
  * out_features_142.  Returns 1 on success; -1, doing nothing, when count is 0
  * or greater than TB_CUDA_NOALLOC_MAX_BATCH; 0 on a NULL pointer or a CUDA
  * error.
- * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * The first call on each device is the set-up: CUDA loads this library's
+ * kernel modules on first use, so that call reserves the array (and the
+ * modules' code) on the device and then looks up the array's device address
+ * (cudaGetSymbolAddress).  Make it at start-up, before a memory pool reserves
+ * the device's memory and before any stream capture.  The address is cached
+ * per device ordinal; after a cudaDeviceReset of that device it is stale, so
+ * do not call this entry point on a device that was reset.
  * All calls on a device share the one array, which keeps the last call's rows:
  * calls that overlap on the GPU (several host threads at once) race.  Each
  * call overwrites every row it reads, so nothing needs clearing between

@@ -4,13 +4,14 @@ y sum (scan_rays in turbinator_c_b200/csrc/onboard_kernel.cu).
 The reference adds the cluster's y values in ray order in float and the
 control law reads only the sign of that sum (onboard_features.cuh:213-239).
 The kernel sums the same values in double, in whatever order its lanes
-combine them, and takes the double sum's sign when |dsum| > 2 n 2^-24 sum|y|;
-otherwise it forms the in-order float sum exactly.  An in-order float sum of
+combine them, and takes the double sum's sign when |dsum| > 2 n 2^-24 sum|y| and
+sum|y| < 2^127; otherwise it forms the in-order float sum exactly.  An in-order float sum of
 n terms differs from the exact sum by at most (n - 1) 2^-24 sum|y| (to first
 order), and the double sum's own error is below 2^-40 of that, so a settled
 sign is the in-order float sum's sign.  Checked here on sums built to cancel:
 mirror-symmetric clusters with small perturbations, values near the corridor
-edge, and long clusters with a wide dynamic range.
+edge, long clusters with a wide dynamic range, and values near FLT_MAX whose
+in-order float sum overflows (the 2^127 cap sends those to the exact path).
 """
 from __future__ import annotations
 
@@ -32,7 +33,7 @@ def kernel_sign(y: np.ndarray, rng: np.random.Generator):
     dsum = float(np.sum(d))
     dabs = float(np.sum(np.abs(d)))
     bound = 2.0 * len(y) * 2.0 ** -24 * dabs
-    if abs(dsum) > bound:
+    if dabs < 2.0 ** 127 and abs(dsum) > bound:
         return 1.0 if dsum > 0 else -1.0
     return None
 
@@ -55,6 +56,14 @@ def _cases(rng: np.random.Generator):
         n = int(rng.integers(2, 64))
         y = rng.uniform(3.4, CORRIDOR_Y, n).astype(np.float32) * rng.choice([-1, 1], n).astype(np.float32)
         yield y
+    # magnitudes near FLT_MAX: the in-order float sum can overflow to +-inf
+    # while the double sum stays finite with the other sign
+    big = np.float32(3.4e38)
+    yield np.array([big, big, -big, -big, -big], np.float32)
+    yield np.array([-big, -big, big, big, big], np.float32)
+    for _ in range(200):
+        n = int(rng.integers(2, 16))
+        yield (rng.uniform(1.0e38, 3.4e38, n) * rng.choice([-1.0, 1.0], n)).astype(np.float32)
 
 
 def test_settled_sign_is_the_in_order_float_sums_sign():
@@ -66,7 +75,16 @@ def test_settled_sign_is_the_in_order_float_sums_sign():
             fallback += 1
             continue
         settled += 1
-        s = in_order_float_sum(y)
+        with np.errstate(over="ignore"):
+            s = in_order_float_sum(y)
         assert s != 0 and np.sign(s) == sign, f"n={len(y)}: settled {sign}, in-order float sum {s!r}"
     # both branches are exercised
     assert settled > 1000 and fallback > 100, (settled, fallback)
+
+
+def test_overflowing_float_sum_takes_the_exact_path():
+    big = np.float32(3.4e38)
+    y = np.array([big, big, -big, -big, -big], np.float32)
+    with np.errstate(over="ignore"):
+        assert in_order_float_sum(y) == np.inf          # while the exact sum is negative
+    assert kernel_sign(y, np.random.default_rng(0)) is None

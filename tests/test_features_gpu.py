@@ -294,20 +294,52 @@ def test_multi_device_handle_rejects_bad_devices():
     check_features(run_device(obs, mission, cams), oracle.features(obs, mission, cams), "after bad multi create")
 
 
-def test_host_abi_reports_pipeline_timeout_once():
-    """The kernels' status word is per device and sticky until read: a
-    pipeline whose bounded waits expired makes the next host call fail with
-    the stage-named message, and the call after it succeeds."""
+def test_pipeline_timeout_is_reported_only_on_its_own_stream():
+    """Each stream has its own status word: a launch whose bounded waits
+    expire (one aircraft's copies withheld, 20 ms limit) on stream A is
+    reported by tb_cuda_synchronize(A) alone, once.  A handle working on
+    another host thread meanwhile and afterwards, and callers synchronising
+    other streams, see no failure."""
+    import threading
+
     obs, mission, cams, _ = tb.generate(32, 0, 16)
     d_obs, d_mis, d_cam = _dev(obs), _dev(mission), _dev(cams)
     d_out = torch.zeros((16, 142), device="cuda")
-    assert tb.take_status() == 0
-    assert tb.launch(d_obs, d_mis, d_cam, d_out, 16, None, wait_ns=20_000_000, stall_sample=3) == 1
-    torch.cuda.synchronize()
-    out = np.zeros((16, 142), np.float32)
-    with tb.FeatureBatch(0, 16) as fb:
-        assert fb.extract(obs, mission, cams, 16, out) == 0
-        assert "feature pipeline wait timed out" in fb.error()
-        assert fb.extract(obs, mission, cams, 16, out) == 1, fb.error()
-        assert fb.error() == ""
-    check_features(out, oracle.features(obs, mission, cams), "after reported timeout")
+    expected = oracle.features(obs, mission, cams)
+    stream_a, stream_b = torch.cuda.Stream(), torch.cuda.Stream()
+    assert tb.take_status(stream_a) == 0 and tb.take_status(stream_b) == 0 and tb.take_status() == 0
+    stalled = threading.Event()
+    results = {}
+
+    def caller_a():
+        torch.cuda.set_device(0)
+        ok = tb.launch(d_obs, d_mis, d_cam, d_out, 16, stream_a, wait_ns=20_000_000, stall_sample=3)
+        stream_a.synchronize()  # the expiry is recorded in A's word by now
+        results["a_launch"] = ok
+        stalled.set()
+
+    def caller_b():
+        torch.cuda.set_device(0)
+        out = np.zeros((16, 142), np.float32)
+        calls = []
+        with tb.FeatureBatch(0, 16) as fb:
+            calls.append(fb.extract(obs, mission, cams, 16, out))   # while A's kernel waits
+            stalled.wait(timeout=30)
+            calls.append(fb.extract(obs, mission, cams, 16, out))   # after A's expiry
+            results["b_error"] = fb.error()
+        results["b_calls"] = calls
+        results["b_out"] = out
+
+    threads = [threading.Thread(target=caller_a), threading.Thread(target=caller_b)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=60)
+    assert results["a_launch"] == 1
+    assert results["b_calls"] == [1, 1], results.get("b_error")
+    check_features(results["b_out"], expected, "handle beside a timed-out stream")
+    assert tb.tb_cuda_synchronize(stream_b) == 1
+    assert tb.tb_cuda_synchronize(None) == 1
+    assert tb.tb_cuda_synchronize(stream_a) == 0      # reported to its own stream
+    assert tb.tb_cuda_synchronize(stream_a) == 1      # once
+    check_features(run_device(obs, mission, cams, stream=stream_a), expected, "stream A after its timeout")

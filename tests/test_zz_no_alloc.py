@@ -56,3 +56,40 @@ def test_noalloc_entry_rejects_sizes_beyond_its_maximum():
     assert tb.tb_cuda_extract_features_host_noalloc(obs, mission, cams, 0, out) == -1
     assert not out.any()
     assert tb.tb_cuda_extract_features_host_noalloc(obs, mission, None, 4, out) == 0
+
+
+_FIRST_CALL = r"""
+import sys
+import numpy as np
+import torch
+sys.path.insert(0, sys.argv[1])
+import turbinator_c_b200 as tb
+torch.cuda.set_device(0)
+torch.cuda.init()
+obs, mission, cams, _ = tb.generate(34, 0, 8)
+out = np.zeros((8, 142), np.float32)
+torch.cuda.synchronize()
+before, _ = torch.cuda.mem_get_info()
+assert tb.tb_cuda_extract_features_host_noalloc(obs, mission, cams, 8, out) == 1
+after_first, _ = torch.cuda.mem_get_info()
+assert tb.tb_cuda_extract_features_host_noalloc(obs, mission, cams, 8, out) == 1
+after_second, _ = torch.cuda.mem_get_info()
+print(before - after_first, after_first - after_second)
+"""
+
+
+def test_first_call_in_a_fresh_process_reserves_the_array():
+    """Modules load lazily: in a fresh process the first call on a device is
+    what reserves the fixed array (and the kernels' code) there, which is why
+    callers make it at start-up; the next call reserves nothing."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    run = subprocess.run([sys.executable, "-c", _FIRST_CALL, root], capture_output=True, text=True, timeout=300)
+    assert run.returncode == 0, run.stderr[-2000:]
+    first, second = (int(v) for v in run.stdout.split()[-2:])
+    print(f"first no-alloc call reserved {first} bytes of device memory; the second {second}")
+    assert first >= 2_149_376, first   # at least the staging array
+    assert second == 0, second

@@ -95,7 +95,7 @@ def load_library() -> ctypes.CDLL:
           [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_launch", _c.c_int,
           [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
-    _bind(lib, "tb_features_status_take", _c.c_int, [_vp, _c.POINTER(_c.c_uint)])
+    _bind(lib, "tb_status_take", _c.c_int, [_vp, _c.POINTER(_c.c_uint)])
     _bind(lib, "tb_features_staged_config", _c.c_int,
           [_c.POINTER(_c.c_int)] * 5)
     _lib = lib
@@ -241,9 +241,9 @@ def launch_actor_inputs(obs, mission, cameras, tactical, prior, proprio, mission
 
 
 def take_status(stream=None) -> int:
-    """Read and clear the current device's kernel status word (0 = clean)."""
+    """Read and clear `stream`'s kernel status word on the current device (0 = clean)."""
     value = _c.c_uint(0)
-    if not load_library().tb_features_status_take(_stream_handle(stream), _c.byref(value)):
+    if not load_library().tb_status_take(_stream_handle(stream), _c.byref(value)):
         raise RuntimeError("could not read the feature kernel status word")
     return value.value
 

@@ -33,7 +33,8 @@
  * the launch ended with its slowest SMs, 1.75 ms against 1.47 ms at 65,536
  * aircraft (runs of 1, 3, 4 and 8: 1.52, 1.50, 1.53 and 1.58 ms).
  * Every mbarrier wait is bounded (about one second); on expiry the kernel
- * records a status bit that tb_cuda_synchronize() reports, drains its own
+ * ORs a bit into the status word of the stream it was launched on
+ * (tb_status.cu), which tb_cuda_synchronize(stream) reports, drains its own
  * outstanding copies (bounded again) and exits.
  *
  * Arithmetic follows the reference kernels' expressions (as nvcc compiles
@@ -80,9 +81,6 @@ static_assert(kObsBytes % 16 == 0 && kCameraBytes % 16 == 0 && kStageBytes == 33
 
 constexpr unsigned long long kDefaultWaitNs = 1000000000ull; /* ~1 s per wait */
 
-/* Sticky per-device status word, read and cleared by tb_cuda_synchronize. */
-__device__ unsigned int g_actor_status;
-
 /* Symlog scale of proprioceptive input i (network_gpu.cu:289-295). */
 __device__ __forceinline__ float symlog_scale(int i) {
     float s = 1.0f;
@@ -127,6 +125,7 @@ struct ActorArgs {
     unsigned long long chunk; /* CTA c takes aircraft [c*chunk, (c+1)*chunk) */
     unsigned long long wait_ns;
     long long stall_sample; /* test hook: withhold this aircraft's copies; -1 normally */
+    unsigned int *status;   /* the launching stream's status word */
 };
 
 __global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorArgs a) {
@@ -178,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorAr
             __syncwarp();
         }
         if (!ok) {
-            if (lane == 0) atomicOr(&g_actor_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
+            if (lane == 0) atomicOr(a.status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
             /* Drain this CTA's outstanding copies before exiting (bounded). */
             const unsigned long long lo = k > kStages ? k - kStages : 0;
             for (unsigned long long j = lo; j < k; ++j)
@@ -194,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorAr
         const int s = static_cast<int>(k % kStages);
         const uint32_t phase = static_cast<uint32_t>((k / kStages) & 1);
         if (!__all_sync(0xffffffffu, mbar_wait(full_bar + 8 * s, phase, a.wait_ns))) {
-            if (lane == 0) atomicOr(&g_actor_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
+            if (lane == 0) atomicOr(a.status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
             return;
         }
         const unsigned char *stage = stages + static_cast<size_t>(s) * kStageBytes;
@@ -291,6 +290,8 @@ extern "C" int tb_actor_inputs_launch(const float *obs, const float *mission, co
     a.batch = batch;
     a.wait_ns = (opts && opts->wait_ns) ? opts->wait_ns : kDefaultWaitNs;
     a.stall_sample = opts ? opts->stall_sample : -1;
+    a.status = tb_status_slot(stream);
+    if (!a.status) return 0;
     cudaGetLastError(); /* report this launch only */
     /* runs of up to kMaxChunk aircraft, but no fewer CTAs than fit at once */
     const unsigned long long resident = static_cast<unsigned long long>(g_resident[dev]);
@@ -299,24 +300,6 @@ extern "C" int tb_actor_inputs_launch(const float *obs, const float *mission, co
     const unsigned long long grid = (batch + a.chunk - 1) / a.chunk;
     actor_inputs_kernel<<<static_cast<unsigned int>(grid), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(a);
     return cudaGetLastError() == cudaSuccess;
-}
-
-extern "C" int tb_actor_status_take(void *stream, unsigned int *status) {
-    unsigned int value = 0;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (cudaMemcpyFromSymbolAsync(&value, g_actor_status, sizeof(value), 0, cudaMemcpyDeviceToHost, s) !=
-            cudaSuccess ||
-        cudaStreamSynchronize(s) != cudaSuccess)
-        return 0;
-    if (value) {
-        static const unsigned int zero = 0;
-        if (cudaMemcpyToSymbolAsync(g_actor_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) !=
-                cudaSuccess ||
-            cudaStreamSynchronize(s) != cudaSuccess)
-            return 0;
-    }
-    if (status) *status = value;
-    return 1;
 }
 
 extern "C" int tb_cuda_prepare_actor_inputs_device(const float *device_obs, const float *device_mission,

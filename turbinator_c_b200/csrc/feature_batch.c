@@ -15,8 +15,10 @@
  *    chunk overlaps the DMA and kernel of the previous one and several lanes
  *    copy in parallel; the driver's own pageable copy runs on one thread at
  *    a fraction of PCIe speed.  Small pageable calls use the driver's path.
- *  - After the last copy the kernels' pipeline status word is checked; a
- *    timed-out pipeline fails the call with a stage-named message.
+ *  - After the last copy the status words of the lane's own streams are
+ *    checked (each stream has its own, tb_status.cu, so another handle's or
+ *    thread's timeout is never reported here); a timed-out pipeline fails
+ *    the call with a stage-named message.
  * Error strings keep the reference's "stage: cuda error" form and stage
  * names (features.cu:20-25,70-87).
  */
@@ -382,17 +384,20 @@ static void *job_main(void *arg) {
     const int used = job->count > chunk_rows ? 2 : 1;
     job->lane->status[0] = job->lane->status[1] = 0;
     for (int b = 0; b < used; ++b)
-        if (!job->stage && !tb_features_status_enqueue(job->lane->streams[b], &job->lane->status[b]))
+        if (!job->stage && !tb_status_enqueue(job->lane->streams[b], &job->lane->status[b]))
             job_fail(job, "synchronize features", cudaGetLastError());
     /* leave nothing in flight that reads or writes the caller's buffers */
     for (int b = 0; b < used; ++b) {
         st = cudaStreamSynchronize(job->lane->streams[b]);
         if (st != cudaSuccess) job_fail(job, "synchronize features", st);
     }
-    if (!job->stage && (job->lane->status[0] | job->lane->status[1])) {
-        tb_features_status_clear(job->lane->streams[0]);
-        job->stage = "synchronize features: feature pipeline wait timed out";
-    }
+    int timed_out = 0;
+    for (int b = 0; b < used; ++b)
+        if (job->lane->status[b]) {
+            tb_status_clear(job->lane->streams[b]); /* report each expiry once */
+            timed_out = 1;
+        }
+    if (!job->stage && timed_out) job->stage = "synchronize features: feature pipeline wait timed out";
     return NULL;
 }
 

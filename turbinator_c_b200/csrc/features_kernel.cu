@@ -43,7 +43,8 @@
  *    and only in-range bins carry the lg2 approximation error (well inside
  *    the 1e-6 absolute / 1e-5 relative tolerance of the parity tests).
  *  - Every mbarrier wait is bounded (about one second of %globaltimer);
- *    on expiry the kernel records a status bit that tb_cuda_synchronize()
+ *    on expiry the kernel ORs a bit into the status word of the stream it
+ *    was launched on (tb_status.cu), which tb_cuda_synchronize(stream)
  *    reports, drains its own outstanding copies (bounded again) and exits.
  */
 #include <cuda_runtime.h>
@@ -93,10 +94,6 @@ static_assert(Ring<false>::stage_bytes == 33024 && Ring<true>::stage_bytes == 82
 constexpr float kInvLog2_121 = 0.14453241315894394f;
 
 constexpr unsigned long long kDefaultWaitNs = 1000000000ull; /* ~1 s per wait */
-
-/* ------------------------------------------------------------------ */
-/* Sticky per-device status word, read and cleared by tb_cuda_synchronize. */
-__device__ unsigned int g_feature_status;
 
 using namespace tb_pipe; /* staging primitives, tb_pipeline.cuh */
 
@@ -211,6 +208,7 @@ struct StagedArgs {
     unsigned long long chunk; /* > 0: CTA c takes aircraft [c*chunk, (c+1)*chunk); 0: grid-stride */
     unsigned long long wait_ns;
     long long stall_sample; /* test hook: >= 0 withholds that sample's copies */
+    unsigned int *status;   /* the launching stream's status word */
 };
 
 template <bool kF32Cam>
@@ -273,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
             __syncwarp();
         }
         if (!ok) {
-            if (lane == 0) atomicOr(&g_feature_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
+            if (lane == 0) atomicOr(a.status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
             /* Drain this CTA's outstanding copies before exiting (bounded). */
             const unsigned long long issued = k;
             const unsigned long long lo = issued > R::stages ? issued - R::stages : 0;
@@ -294,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
         const int s = static_cast<int>(k % R::stages);
         const uint32_t phase = static_cast<uint32_t>((k / R::stages) & 1);
         if (!__all_sync(0xffffffffu, mbar_wait(full_bar + 8 * s, phase, a.wait_ns))) {
-            if (lane == 0) atomicOr(&g_feature_status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
+            if (lane == 0) atomicOr(a.status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
             return;
         }
         const unsigned char *stage = stages + static_cast<size_t>(s) * R::stage_bytes;
@@ -517,7 +515,13 @@ static int launch_features(const float *obs, const float *mission, const void *c
     const int force_direct = opts && opts->force_direct;
     const bool staged = !force_direct && aligned(obs, 16) && (!cameras || aligned(cameras, 16));
     if (staged) {
+        unsigned int *status = tb_status_slot(stream);
+        if (!status) {
+            if (launch_error) *launch_error = static_cast<int>(cudaErrorInvalidDevice);
+            return 0;
+        }
         StagedArgs args;
+        args.status = status;
         args.obs = obs;
         args.mission = mission;
         args.cameras = cameras;
@@ -574,37 +578,6 @@ extern "C" int tb_features_launch(const float *obs, const float *mission,
     return tb_features_launch_checked(obs, mission, cameras, features, batch, stream, opts, nullptr);
 }
 
-extern "C" int tb_features_status_take(void *stream, unsigned int *status) {
-    unsigned int value = 0;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (cudaMemcpyFromSymbolAsync(&value, g_feature_status, sizeof(value), 0,
-                                  cudaMemcpyDeviceToHost, s) != cudaSuccess)
-        return 0;
-    if (cudaStreamSynchronize(s) != cudaSuccess) return 0;
-    if (value) {
-        static const unsigned int zero = 0;
-        if (cudaMemcpyToSymbolAsync(g_feature_status, &zero, sizeof(zero), 0,
-                                    cudaMemcpyHostToDevice, s) != cudaSuccess)
-            return 0;
-        if (cudaStreamSynchronize(s) != cudaSuccess) return 0;
-    }
-    if (status) *status = value;
-    return 1;
-}
-
-extern "C" int tb_features_status_enqueue(void *stream, unsigned int *host_word) {
-    return cudaMemcpyFromSymbolAsync(host_word, g_feature_status, sizeof(unsigned int), 0,
-                                     cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)) == cudaSuccess;
-}
-
-extern "C" int tb_features_status_clear(void *stream) {
-    static const unsigned int zero = 0;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    return cudaMemcpyToSymbolAsync(g_feature_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) ==
-               cudaSuccess &&
-           cudaStreamSynchronize(s) == cudaSuccess;
-}
-
 extern "C" int tb_features_staged_config(int *blocks_per_sm, int *sms, int *smem_bytes,
                                          int *threads, int *stages) {
     int dev = 0;
@@ -629,13 +602,14 @@ extern "C" int tb_cuda_extract_features_device(const float *device_obs, const fl
                               batch_size, stream, nullptr);
 }
 
+/* Waits for `stream`, then reads and clears the status word that the
+ * kernels launched on that stream write: 0 if a pipeline wait of any of them
+ * expired (reported once), or on a CUDA error. */
 extern "C" int tb_cuda_synchronize(void *stream) {
     if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return 0;
-    unsigned int features = 0, onboard = 0, actor = 0;
-    if (!tb_features_status_take(stream, &features) || !tb_onboard_status_take(stream, &onboard) ||
-        !tb_actor_status_take(stream, &actor))
-        return 0;
-    return (features | onboard | actor) == 0;
+    unsigned int status = 0;
+    if (!tb_status_take(stream, &status)) return 0;
+    return status == 0;
 }
 
 /* ---- additive entry point: FP32 cameras ---- */

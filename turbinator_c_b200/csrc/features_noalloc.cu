@@ -13,8 +13,12 @@
  * The array's name is only a host-side stand-in in host code; the device
  * address is looked up once per device with cudaGetSymbolAddress (with that
  * device current) on the first call, and that address is what the kernel
- * receives.  This file calls no cudaMalloc, cudaFree or other allocating
- * routine.
+ * receives.  CUDA loads modules lazily, so that first call is also when the
+ * array (and the kernels' code) is reserved on the device: callers make it at
+ * start-up, before a memory pool takes the device's memory and before any
+ * stream capture.  The cached address belongs to the device's context at the
+ * time of the look-up and is stale after a cudaDeviceReset.  This file calls
+ * no cudaMalloc, cudaFree or other allocating routine.
  */
 #include <cuda_runtime.h>
 
@@ -101,6 +105,6 @@ extern "C" int tb_cuda_extract_features_host_noalloc(const float *obs_4148, cons
     }
     if (cudaStreamSynchronize(s) != cudaSuccess) return 0;
     unsigned int pipeline = 0;
-    if (!tb_features_status_take(stream, &pipeline) || pipeline) return 0;
+    if (!tb_status_take(stream, &pipeline) || pipeline) return 0;
     return 1;
 }

@@ -43,6 +43,7 @@
 #include <stdint.h>
 
 #include "tb_features_internal.h"
+#include "tb_pipeline.cuh"
 #include "turbinator/training/cuda_features.h"
 
 namespace {
@@ -174,9 +175,6 @@ __device__ void build_ray_tables(RayTables &t) {
     }
 }
 
-/* Sticky status word of this file's kernels (bit 1: a staging wait expired). */
-__device__ unsigned int g_onboard_status;
-
 /* Per-warp shared memory: one staged LiDAR block (the 1,536 controller rays
  * of one aircraft, in ray order) and pass 1's corridor-centre x per ray (+inf
  * outside the corridor), which pass 2 reads back.  A single block per warp
@@ -196,34 +194,7 @@ struct alignas(16) WarpSlot {
 static_assert(sizeof(WarpSlot) % 16 == 0 && offsetof(WarpSlot, ranges) == 0 && (kRays / 2 * 4) % 16 == 0,
               "bulk-copy destinations must be 16-byte aligned");
 
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-
-/* Bounded wait (about one second of %globaltimer); false on expiry. */
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
-    if (mbar_try_wait(bar, parity)) return true;
-    unsigned long long t0, t1;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    for (;;) {
-        for (int i = 0; i < 32; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-        if (t1 - t0 > limit_ns) return false;
-    }
-}
+using namespace tb_pipe; /* mbarriers, bounded waits, bulk copies: tb_pipeline.cuh */
 
 /* Stage aircraft `row`'s two LiDAR blocks (heads 0 and 1, elevations 0..5)
  * into slot.ranges.  16-byte aligned rows take two 1-D bulk copies completing
@@ -235,25 +206,15 @@ __device__ __forceinline__ void stage_rays(WarpSlot &slot, const float *obs_row,
     float *dst = slot.ranges;
     if (bulk) {
         if (lane == 0) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                         "r"(2u * kHeadBlockBytes)
-                         : "memory");
-            asm volatile(
-                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                    smem_addr(dst)),
-                "l"(obs_row + 48), "r"(kHeadBlockBytes), "r"(bar)
-                : "memory");
-            asm volatile(
-                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                    smem_addr(dst + kRays / 2)),
-                "l"(obs_row + 48 + 2048), "r"(kHeadBlockBytes), "r"(bar)
-                : "memory");
+            fence_proxy_async_shared();
+            mbar_arrive_expect_tx(bar, 2u * kHeadBlockBytes);
+            bulk_load(smem_addr(dst), obs_row + 48, kHeadBlockBytes, bar);
+            bulk_load(smem_addr(dst + kRays / 2), obs_row + 48 + 2048, kHeadBlockBytes, bar);
         }
     } else {
         for (int i = lane; i < kRays; i += 32) dst[i] = __ldg(obs_row + 48 + (i >= kRays / 2 ? 2048 - kRays / 2 : 0) + i);
         __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+        if (lane == 0) mbar_arrive(bar);
     }
 }
 
@@ -382,7 +343,11 @@ __device__ RayStats scan_rays(const RayTables &t, WarpSlot &slot, const float *r
     }
     s.cluster_count = count;
     const double bound = 2.0 * static_cast<double>(count) * 0x1.0p-24 * dabs;
-    if (fabs(dsum) > bound) {
+    /* The bound assumes no in-order float partial sum overflows: every partial
+     * sum is at most sum|y| (1 + n 2^-24) in magnitude, below FLT_MAX when
+     * sum|y| < 2^127 (n <= 1,536).  Larger or non-finite sums take the exact
+     * path. */
+    if (dabs < 0x1.0p127 && fabs(dsum) > bound) {
         /* Sign settled: the in-order float sum has the sign of dsum. */
         s.cluster_y_sum = dsum > 0.0 ? 1.0f : -1.0f;
     } else {
@@ -906,7 +871,8 @@ __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__r
                                                                 float *__restrict__ prior_out,
                                                                 unsigned long long batch,
                                                                 unsigned long long wait_ns,
-                                                                long long stall_sample) {
+                                                                long long stall_sample,
+                                                                unsigned int *__restrict__ status) {
     __shared__ RayTables tables;
     extern __shared__ __align__(128) unsigned char dyn[];
     build_ray_tables(tables);
@@ -915,8 +881,8 @@ __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__r
     WarpSlot &slot = reinterpret_cast<WarpSlot *>(dyn)[warp];
     ChunkState &chunk = *reinterpret_cast<ChunkState *>(dyn + sizeof(WarpSlot) * kWarps);
     if (lane == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&slot.bar)) : "memory");
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_init(smem_addr(&slot.bar), 1);
+        fence_mbar_init();
     }
     __syncthreads();
 
@@ -961,7 +927,7 @@ __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__r
                 stage_rays(slot, obs + a * kObsDim, bulk, lane);
             /* all lanes take the same branch, even if the copy lands at the deadline */
             if (!__all_sync(kFull, mbar_wait(smem_addr(&slot.bar), seq & 1, wait_ns))) {
-                if (lane == 0) atomicOr(&g_onboard_status, 1u);
+                if (lane == 0) atomicOr(status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
                 failed = true;
                 break;
             }
@@ -1021,24 +987,6 @@ int g_sms[kMaxDevices];
 
 } /* namespace */
 
-extern "C" int tb_onboard_status_take(void *stream, unsigned int *status) {
-    unsigned int value = 0;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (cudaMemcpyFromSymbolAsync(&value, g_onboard_status, sizeof(value), 0, cudaMemcpyDeviceToHost, s) !=
-            cudaSuccess ||
-        cudaStreamSynchronize(s) != cudaSuccess)
-        return 0;
-    if (value) {
-        static const unsigned int zero = 0;
-        if (cudaMemcpyToSymbolAsync(g_onboard_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) !=
-                cudaSuccess ||
-            cudaStreamSynchronize(s) != cudaSuccess)
-            return 0;
-    }
-    if (status) *status = value;
-    return 1;
-}
-
 /* Both launches; opts may be NULL (its wait_ns and stall_sample fields are
  * honoured: a test withholds one scanning aircraft's staging copy so the
  * bounded wait expires). */
@@ -1065,13 +1013,15 @@ extern "C" int tb_onboard_launch(const float *device_obs, const float *device_mi
     }
     const unsigned long long wait_ns = (opts && opts->wait_ns) ? opts->wait_ns : kWaitNs;
     const long long stall_sample = opts ? opts->stall_sample : -1;
+    unsigned int *status = tb_status_slot(stream);
+    if (!status) return 0;
     cudaGetLastError(); /* report these launches only */
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     /* scans: one CTA per SM (shared memory admits one) */
     unsigned long long grid = static_cast<unsigned long long>(g_sms[dev]);
     if (grid > batch_size) grid = batch_size;
     onboard_scan_kernel<<<static_cast<unsigned int>(grid), kThreads, kDynSmem, s>>>(
-        device_obs, device_mission, device_prior_15, batch_size, wait_ns, stall_sample);
+        device_obs, device_mission, device_prior_15, batch_size, wait_ns, stall_sample, status);
     /* control law: one thread per aircraft */
     const unsigned long long control_grid = (batch_size + kControlThreads - 1) / kControlThreads;
     onboard_control_kernel<<<static_cast<unsigned int>(control_grid), kControlThreads, 0, s>>>(

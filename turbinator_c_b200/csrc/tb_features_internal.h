@@ -18,7 +18,7 @@ enum {
     TB_FEATURE_DIM = 142
 };
 
-/* Status bits recorded by the kernels in a per-device word. */
+/* Status bits recorded by the kernels in their stream's status word. */
 enum { TB_FEATURE_STATUS_WAIT_TIMEOUT = 1u };
 
 typedef struct tb_features_launch_opts {
@@ -49,24 +49,26 @@ int tb_features_launch_f32cam(const float *obs, const float *mission, const floa
                               float *features, size_t batch, void *stream,
                               const tb_features_launch_opts *opts);
 
-/* Reads (via `stream`) and clears the current device's kernel status word.
- * Returns 1 if the read succeeded; *status receives the bits. */
-int tb_features_status_take(void *stream, unsigned int *status);
+/* Status word of `stream` on the current device (tb_status.cu): the device
+ * address that the kernels launched on that stream receive and OR their
+ * status bits into.  NULL if the device cannot be queried. */
+unsigned int *tb_status_slot(void *stream);
 
-/* Enqueue on `stream` an asynchronous copy of the current device's status
- * word into host_word (page-locked), to be read after the stream drains. */
-int tb_features_status_enqueue(void *stream, unsigned int *host_word);
+/* Reads (via `stream`) and clears `stream`'s status word on the current
+ * device.  Returns 1 if the read succeeded; *status receives the bits. */
+int tb_status_take(void *stream, unsigned int *status);
 
-/* Clear the current device's status word (synchronous on `stream`). */
-int tb_features_status_clear(void *stream);
+/* Enqueue on `stream` an asynchronous copy of its status word into
+ * host_word (page-locked), to be read after the stream drains. */
+int tb_status_enqueue(void *stream, unsigned int *host_word);
+
+/* Clear `stream`'s status word (synchronous on `stream`). */
+int tb_status_clear(void *stream);
 
 /* tb_cuda_extract_onboard_device with launch options (wait_ns and stall_sample
  * are honoured); opts may be NULL. */
 int tb_onboard_launch(const float *obs, const float *mission, float *tactical, float *prior, size_t batch,
                       void *stream, const tb_features_launch_opts *opts);
-
-/* As tb_features_status_take, for the onboard kernel's own status word. */
-int tb_onboard_status_take(void *stream, unsigned int *status);
 
 /* The learner-input streaming kernel alone (tactical and prior already in
  * place), as tb_cuda_prepare_actor_inputs_device launches it after the
@@ -75,9 +77,6 @@ int tb_actor_inputs_launch(const float *obs, const float *mission, const unsigne
                            const float *tactical, const float *prior, float *proprio, float *mission_vec,
                            float *lidar, float *luma, size_t batch, void *stream,
                            const tb_features_launch_opts *opts);
-
-/* As tb_features_status_take, for the learner-input kernel's status word. */
-int tb_actor_status_take(void *stream, unsigned int *status);
 
 /* Launch geometry of the staged kernel on the current device. */
 int tb_features_staged_config(int *blocks_per_sm, int *sms, int *smem_bytes, int *threads,

@@ -69,6 +69,25 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_
         : "memory");
 }
 
+/* The same without a cache hint. */
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+/* Order this thread's earlier generic-proxy shared-memory accesses before
+ * later async-proxy (bulk copy) writes to the same memory. */
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+/* Make initialised mbarriers visible to the async proxy. */
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
 /* 4-byte asynchronous copy (rows that are only 4- or 8-byte aligned). */
 __device__ __forceinline__ void async_load4(uint32_t dst, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
