@@ -41,3 +41,19 @@ def check_features(actual: np.ndarray, expected: np.ndarray, what: str = "") -> 
 def max_lidar_error(actual: np.ndarray, expected: np.ndarray) -> float:
     return float(np.max(np.abs(actual[:, LIDAR].astype(np.float64) - expected[:, LIDAR].astype(np.float64)),
                         initial=0.0))
+
+
+def mismatch_counts(actual: np.ndarray, expected: np.ndarray) -> tuple:
+    """(rows with an exact-class feature that differs in any bit, LiDAR
+    values out of tolerance or non-finite) under the same rules as
+    check_features; (0, 0) is a pass."""
+    a = np.ascontiguousarray(actual, np.float32)
+    e = np.ascontiguousarray(expected, np.float32)
+    if a.shape != e.shape:
+        raise ValueError(f"shape {a.shape} != {e.shape}")
+    exact_rows = int(np.count_nonzero(np.any(a.view(np.uint32)[:, EXACT] != e.view(np.uint32)[:, EXACT], axis=1)))
+    al = a[:, LIDAR].astype(np.float64)
+    el = e[:, LIDAR].astype(np.float64)
+    with np.errstate(invalid="ignore"):
+        bad = ~(np.abs(al - el) <= ABS_TOL + REL_TOL * np.abs(el))
+    return exact_rows, int(np.count_nonzero(bad))

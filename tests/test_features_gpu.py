@@ -64,10 +64,12 @@ def test_seeded_goldens(name):
     check_features(run_device(obs, mission, cams), expected, name)
 
 
-def test_edge_values_with_and_without_cameras():
+@pytest.mark.parametrize("kernel", [-1, 1])
+def test_edge_values_with_and_without_cameras(kernel):
     g = np.load(os.path.join(GOLDEN, "edge_cases.npz"))
-    check_features(run_device(g["obs"], g["mission"], g["cameras"]), g["features"], "edge")
-    check_features(run_device(g["obs"], g["mission"], None), g["features_no_camera"], "edge/no-camera")
+    check_features(run_device(g["obs"], g["mission"], g["cameras"], flat=kernel), g["features"], "edge")
+    check_features(run_device(g["obs"], g["mission"], None, flat=kernel), g["features_no_camera"],
+                   "edge/no-camera")
 
 
 def test_reference_training_facts_on_gpu():
@@ -101,13 +103,18 @@ def test_config4_stress_quarters_full_size():
     assert np.all(d == d[0, 0])                                                   # (d) identical
 
 
-# 296 CTAs are resident at once: batches past that go in runs of ceil(B / 296) aircraft per CTA
-# (at most 8), so 297, 593, 2,367, 2,369 and 9,001 end in a shorter run
+# Staged kernel: 296 CTAs are resident at once, and batches past that go in runs of
+# ceil(B / 296) aircraft per CTA (at most 8), so 297, 593, 2,367, 2,369 and 9,001 end in a
+# shorter run.  Batches of up to 16 aircraft per SM (2,368) take the flat kernel by default;
+# each size runs on the default choice and on both kernels forced.
+@pytest.mark.parametrize("kernel", [0, -1, 1])
 @pytest.mark.parametrize("batch", [1, 2, 3, 7, 147, 148, 149, 295, 296, 297, 592, 593, 1023, 1025,
                                    2367, 2368, 2369, 9001])
-def test_ragged_batch_sizes(batch):
+def test_ragged_batch_sizes(batch, kernel):
     obs, mission, cams, _ = tb.generate(21, 0, batch)
-    check_features(run_device(obs, mission, cams), oracle.features(obs, mission, cams), f"B={batch}")
+    opts = {"flat": kernel} if kernel else {}
+    check_features(run_device(obs, mission, cams, **opts), oracle.features(obs, mission, cams),
+                   f"B={batch} flat={kernel}")
 
 
 @pytest.mark.parametrize("grid_limit", [1, 2, 5])

@@ -53,14 +53,15 @@ def special_batch(seed: int, n: int, rate: float, odd_attitudes: bool = True):
     return obs, mission, cams
 
 
+@pytest.mark.parametrize("kernel", [-1, 1])   # staged, flat
 @pytest.mark.parametrize("seed,rate", [(1, 0.02), (2, 0.2), (3, 0.6)])
-def test_features_on_special_values(seed, rate):
+def test_features_on_special_values(seed, rate, kernel):
     obs, mission, cams = special_batch(seed, 2048, rate)
     d = [torch.from_numpy(x).cuda() for x in (obs, mission, cams)]
     out = torch.full((2048, 142), float("nan"), device="cuda")
-    assert tb.tb_cuda_extract_features_device(*d, out, 2048, None) == 1
+    assert tb.launch(*d, out, 2048, None, flat=kernel) == 1
     assert tb.tb_cuda_synchronize(None) == 1
-    check_features(out.cpu().numpy(), oracle.features(obs, mission, cams), f"special rate {rate}")
+    check_features(out.cpu().numpy(), oracle.features(obs, mission, cams), f"special rate {rate} flat={kernel}")
 
 
 @pytest.mark.parametrize("seed,rate", [(4, 0.02), (5, 0.2), (6, 0.6)])

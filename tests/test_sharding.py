@@ -69,3 +69,48 @@ def test_two_rank_gather_matches_single_process(tmp_path, total, stress):
     expected = oracle.features(obs, mission, cams)
     assert np.array_equal(gathered.view(np.uint32), expected.view(np.uint32))
     assert float(open(path + ".max").read()) == 2.0
+
+
+def _gather_worker(rank, world, port, total, result_path):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from turbinator_c_b200.shard import SharedHostGather, all_ranks, max_over_ranks_list, sum_over_ranks
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        g = SharedHostGather(total, 142, pin=False)   # no GPU here: plain host copies into the shared file
+        first, count = shard_range(total, rank, world)
+        rows = np.arange(first * 142, (first + count) * 142, dtype=np.float32).reshape(count, 142)
+        g.gather(torch.from_numpy(rows))
+        dist.barrier()
+        ok = rank != 0 or np.array_equal(g.array, np.arange(total * 142, dtype=np.float32).reshape(total, 142))
+        maxes = max_over_ranks_list([rank, -rank])
+        sums = sum_over_ranks([1, rank])
+        everyone = all_ranks({"rank": rank})
+        g.close()
+        if rank == 0:
+            with open(result_path, "w") as f:
+                f.write(repr((bool(ok), maxes, sums, [e["rank"] for e in everyone], os.path.exists(g.path))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total", [(2, 37), (3, 1000)])
+def test_shared_host_gather_assembles_every_slice(tmp_path, world, total):
+    """Each rank writes its own slice into the shared host buffer at its
+    offset; rank 0 then reads the whole batch.  The reductions used by the
+    benchmark's timing and parity counts work over the same ranks, and the
+    shared file is removed on close."""
+    path = str(tmp_path / "gather.txt")
+    mp.spawn(_gather_worker, args=(world, _free_port(), total, path), nprocs=world, join=True)
+    ok, maxes, sums, ranks, left = eval(open(path).read())
+    assert ok
+    assert maxes == [world - 1.0, 0.0]
+    assert sums == [world, sum(range(world))]
+    assert ranks == list(range(world))
+    assert not left

@@ -56,6 +56,7 @@ class LaunchOpts(_c.Structure):
         ("grid_limit", _c.c_int),
         ("wait_ns", _c.c_ulonglong),
         ("stall_sample", _c.c_longlong),
+        ("flat", _c.c_int),
     ]
 
 
@@ -172,7 +173,7 @@ def tb_cuda_extract_features_device_f32cam(obs, mission, cameras_f32, features, 
 
 def launch_f32cam(obs, mission, cameras_f32, features, batch_size: int, stream=None, *,
                   force_direct: bool = False, grid_limit: int = 0) -> int:
-    opts = LaunchOpts(int(force_direct), int(grid_limit), 0, -1)
+    opts = LaunchOpts(int(force_direct), int(grid_limit), 0, -1, 0)
     return load_library().tb_features_launch_f32cam(
         _ptr(obs), _ptr(mission), _ptr(cameras_f32), _ptr(features), batch_size,
         _stream_handle(stream), _c.byref(opts))
@@ -214,10 +215,11 @@ def tb_cuda_extract_features_host_noalloc(obs, mission, cameras, count: int, out
 
 def launch(obs, mission, cameras, features, batch_size: int, stream=None, *,
            force_direct: bool = False, grid_limit: int = 0, wait_ns: int = 0,
-           stall_sample: int = -1) -> int:
+           stall_sample: int = -1, flat: int = 0) -> int:
     """``tb_features_launch`` with explicit options (kernel choice, grid cap,
-    pipeline wait limit, and the test-only stalled-sample hook)."""
-    opts = LaunchOpts(int(force_direct), int(grid_limit), int(wait_ns), int(stall_sample))
+    pipeline wait limit, the test-only stalled-sample hook, and the flat
+    kernel: 0 = by batch size, 1 = always, -1 = never)."""
+    opts = LaunchOpts(int(force_direct), int(grid_limit), int(wait_ns), int(stall_sample), int(flat))
     return load_library().tb_features_launch(
         _ptr(obs), _ptr(mission), _ptr(cameras), _ptr(features), batch_size,
         _stream_handle(stream), _c.byref(opts))
@@ -226,7 +228,7 @@ def launch(obs, mission, cameras, features, batch_size: int, stream=None, *,
 def launch_onboard(obs, mission, tactical, prior, batch_size: int, stream=None, *, wait_ns: int = 0,
                    stall_sample: int = -1) -> int:
     """tb_cuda_extract_onboard_device with the test hook (bounded waits)."""
-    opts = LaunchOpts(0, 0, wait_ns, stall_sample)
+    opts = LaunchOpts(0, 0, wait_ns, stall_sample, 0)
     return load_library().tb_onboard_launch(_ptr(obs), _ptr(mission), _ptr(tactical), _ptr(prior), batch_size,
                                             _stream_handle(stream), _c.byref(opts))
 
@@ -234,7 +236,7 @@ def launch_onboard(obs, mission, tactical, prior, batch_size: int, stream=None, 
 def launch_actor_inputs(obs, mission, cameras, tactical, prior, proprio, mission_vec, lidar, luma, batch_size: int,
                         stream=None, *, wait_ns: int = 0, stall_sample: int = -1) -> int:
     """The learner-input streaming kernel alone (test hook: bounded waits)."""
-    opts = LaunchOpts(0, 0, wait_ns, stall_sample)
+    opts = LaunchOpts(0, 0, wait_ns, stall_sample, 0)
     return load_library().tb_actor_inputs_launch(
         _ptr(obs), _ptr(mission), _ptr(cameras), _ptr(tactical), _ptr(prior), _ptr(proprio), _ptr(mission_vec),
         _ptr(lidar), _ptr(luma), batch_size, _stream_handle(stream), _c.byref(opts))

@@ -95,6 +95,10 @@ constexpr float kInvLog2_121 = 0.14453241315894394f;
 
 constexpr unsigned long long kDefaultWaitNs = 1000000000ull; /* ~1 s per wait */
 
+/* Largest u8 batch, in aircraft per SM, that takes the flat kernel rather
+ * than the staged one. */
+constexpr int kFlatMaxPerSm = 16;
+
 using namespace tb_pipe; /* staging primitives, tb_pipeline.cuh */
 
 /* ------------------------------------------------------------------ */
@@ -167,6 +171,45 @@ __device__ __forceinline__ float camera_feature(unsigned int sum) {
 
 __device__ __forceinline__ uint32_t byte_sum4(uint32_t w, uint32_t acc) {
     return __dp4a(w, 0x01010101u, acc);
+}
+
+/* Byte sum of one camera quadrant from a warp's half image: lane holds the
+ * 16-byte chunks lane, lane+32, lane+64, lane+96 of the half (chunk c in row
+ * c/4, columns 16*(c%4).., so quadrant x = lane bit 1); the result is valid
+ * in every lane, for the lane's quadrant. */
+__device__ __forceinline__ uint32_t quadrant_bytes(const uint4 c0, const uint4 c1, const uint4 c2,
+                                                   const uint4 c3) {
+    uint32_t bytes = 0;
+    bytes = byte_sum4(c0.x, bytes); bytes = byte_sum4(c0.y, bytes);
+    bytes = byte_sum4(c0.z, bytes); bytes = byte_sum4(c0.w, bytes);
+    bytes = byte_sum4(c1.x, bytes); bytes = byte_sum4(c1.y, bytes);
+    bytes = byte_sum4(c1.z, bytes); bytes = byte_sum4(c1.w, bytes);
+    bytes = byte_sum4(c2.x, bytes); bytes = byte_sum4(c2.y, bytes);
+    bytes = byte_sum4(c2.z, bytes); bytes = byte_sum4(c2.w, bytes);
+    bytes = byte_sum4(c3.x, bytes); bytes = byte_sum4(c3.y, bytes);
+    bytes = byte_sum4(c3.z, bytes); bytes = byte_sum4(c3.w, bytes);
+    bytes += __shfl_xor_sync(0xffffffffu, bytes, 1);
+    bytes += __shfl_xor_sync(0xffffffffu, bytes, 4);
+    bytes += __shfl_xor_sync(0xffffffffu, bytes, 8);
+    bytes += __shfl_xor_sync(0xffffffffu, bytes, 16);
+    return bytes;
+}
+
+/* Sector accumulators of a warp's four LiDAR rows: lane holds bins
+ * 4*lane..4*lane+3 of each row, i.e. sector lane/4; reduced over the four
+ * lanes of each sector. */
+__device__ __forceinline__ void lidar_band(const float4 r0, const float4 r1, const float4 r2, const float4 r3,
+                                           float &sum, int &counts) {
+    sum = 0.0f;
+    counts = 0;
+    lidar_bins4(r0, sum, counts);
+    lidar_bins4(r1, sum, counts);
+    lidar_bins4(r2, sum, counts);
+    lidar_bins4(r3, sum, counts);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    counts += __shfl_xor_sync(0xffffffffu, counts, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    counts += __shfl_xor_sync(0xffffffffu, counts, 2);
 }
 
 /* The simulator's camera quantisation (reference src/sim/sensors.c:67 with
@@ -322,18 +365,7 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(empty_bar + 8 * s); /* stage fully read: release it */
-            bytes = byte_sum4(c0.x, bytes); bytes = byte_sum4(c0.y, bytes);
-            bytes = byte_sum4(c0.z, bytes); bytes = byte_sum4(c0.w, bytes);
-            bytes = byte_sum4(c1.x, bytes); bytes = byte_sum4(c1.y, bytes);
-            bytes = byte_sum4(c1.z, bytes); bytes = byte_sum4(c1.w, bytes);
-            bytes = byte_sum4(c2.x, bytes); bytes = byte_sum4(c2.y, bytes);
-            bytes = byte_sum4(c2.z, bytes); bytes = byte_sum4(c2.w, bytes);
-            bytes = byte_sum4(c3.x, bytes); bytes = byte_sum4(c3.y, bytes);
-            bytes = byte_sum4(c3.z, bytes); bytes = byte_sum4(c3.w, bytes);
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, 1);
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, 4);
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, 8);
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, 16);
+            bytes = quadrant_bytes(c0, c1, c2, c3);
         } else {
             /* float4 chunk c (c = lane, lane+32, ...) sits in row c/16,
              * columns 4*(c%16).., so quadrant x = lane bit 3. */
@@ -351,16 +383,9 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
             luma += __shfl_xor_sync(0xffffffffu, luma, 16);
         }
 
-        float sum = 0.0f;
-        int counts = 0;
-        lidar_bins4(r0, sum, counts);
-        lidar_bins4(r1, sum, counts);
-        lidar_bins4(r2, sum, counts);
-        lidar_bins4(r3, sum, counts);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        counts += __shfl_xor_sync(0xffffffffu, counts, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        counts += __shfl_xor_sync(0xffffffffu, counts, 2);
+        float sum;
+        int counts;
+        lidar_band(r0, r1, r2, r3, sum, counts);
 
         float *f = a.features + sample * kFeatureDim;
         if ((lane & 3) == 0)
@@ -373,6 +398,53 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
         }
         if (t < 62) f[t] = scalar;
     }
+}
+
+/* ------------------------------------------------------------------ */
+/* Flat kernel for u8 batches too small to fill the staged kernel's rings
+ * (1,024 aircraft): one 256-thread CTA per aircraft, and
+ * each warp loads its share -- the staged kernel's consumer-warp roles --
+ * straight into registers with 128-bit streaming loads (32 KB of a CTA's
+ * 33 KB in flight at once, several CTAs per SM), so the whole of a small
+ * batch is requested at once instead of trickling through 3-stage rings in
+ * runs of aircraft.  Same arithmetic as the staged kernel; no waits,
+ * so no status word. */
+__global__ void __launch_bounds__(kConsumerWarps * 32) features_flat_kernel(const float *__restrict__ obs,
+                                                                           const float *__restrict__ mission,
+                                                                           const unsigned char *__restrict__ cameras,
+                                                                           float *__restrict__ features) {
+    const unsigned long long sample = blockIdx.x;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int head = warp >> 2, el_sector = warp & 3; /* LiDAR rows 4w..4w+3 */
+    const int cam = warp >> 1, qy = warp & 1;         /* camera half-image w */
+    const float *o = obs + sample * kObsDim;
+    const float *m = mission + sample * kMissionDim;
+
+    const float4 *rows = reinterpret_cast<const float4 *>(o + kLidarOffset) + (head * 16 + el_sector * 4) * 32 + lane;
+    const float4 r0 = __ldcs(rows), r1 = __ldcs(rows + 32), r2 = __ldcs(rows + 64), r3 = __ldcs(rows + 96);
+    uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0, c2 = c0, c3 = c0;
+    if (cameras) {
+        const uint4 *half = reinterpret_cast<const uint4 *>(cameras + sample * kCameraBytes) + cam * 256 +
+                            qy * 128 + lane;
+        c0 = __ldcs(half);
+        c1 = __ldcs(half + 32);
+        c2 = __ldcs(half + 64);
+        c3 = __ldcs(half + 96);
+    }
+    const int t = warp * 32 + lane;
+    float scalar = 0.0f;
+    if (t < 62) scalar = scalar_feature(t, o, m);
+
+    const uint32_t bytes = quadrant_bytes(c0, c1, c2, c3);
+    float sum;
+    int counts;
+    lidar_band(r0, r1, r2, r3, sum, counts);
+
+    float *f = features + sample * kFeatureDim;
+    if ((lane & 3) == 0) f[62 + head * 32 + el_sector * 8 + (lane >> 2)] = lidar_sector_mean(sum, counts);
+    if (lane == 0 || lane == 2) f[126 + cam * 4 + qy * 2 + (lane >> 1)] = camera_feature(bytes);
+    if (t < 62) f[t] = scalar;
 }
 
 /* ------------------------------------------------------------------ */
@@ -513,8 +585,20 @@ static int launch_features(const float *obs, const float *mission, const void *c
      * persists and still fails it). */
     cudaGetLastError();
     const int force_direct = opts && opts->force_direct;
-    const bool staged = !force_direct && aligned(obs, 16) && (!cameras || aligned(cameras, 16));
-    if (staged) {
+    const bool aligned_rows = !force_direct && aligned(obs, 16) && (!cameras || aligned(cameras, 16));
+    const int flat_choice = opts ? opts->flat : 0;
+    /* the test hooks (grid cap, withheld copies) act on the staged kernel */
+    const bool limited_grid = opts && (opts->grid_limit > 0 || opts->stall_sample >= 0);
+    /* small u8 batches take the flat kernel; the staged kernel's rings only
+     * pay off once every SM has many aircraft to stream */
+    const unsigned long long flat_max = static_cast<unsigned long long>(kFlatMaxPerSm) *
+                                        static_cast<unsigned long long>(info->sms);
+    const bool flat = !kF32Cam && aligned_rows && !limited_grid && flat_choice >= 0 &&
+                      (flat_choice > 0 || batch <= flat_max);
+    if (flat) {
+        features_flat_kernel<<<static_cast<unsigned int>(batch), kConsumerWarps * 32, 0, s>>>(
+            obs, mission, static_cast<const unsigned char *>(cameras), features);
+    } else if (aligned_rows) {
         unsigned int *status = tb_status_slot(stream);
         if (!status) {
             if (launch_error) *launch_error = static_cast<int>(cudaErrorInvalidDevice);
