@@ -288,7 +288,8 @@ def time_config1(stream, dev):
     """BASELINE config 1 (seed 1, 1,024 aircraft): launch latency.  Its
     34.4 MB of inputs fit in the 126 MB L2, so device time is reported
     L2-resident (back to back) and with L2 flushed before every launch, each
-    the median of 20 launches timed with CUDA events queued back to back.
+    the median of 20 launches timed with CUDA events queued back to back
+    behind a GPU sleep (so the events bracket GPU work, not host latency).
     Two flushes: a 256 MiB buffer rewritten (the L2 then holds ~126 MB of
     dirty lines, which the launch's own reads must write back to HBM first),
     and the same followed by a read of the buffer (the L2 then holds clean
@@ -316,10 +317,12 @@ def time_config1(stream, dev):
     torch.cuda.synchronize(dev)
 
     def device_ms(call, flushed):
-        # all 20 (flush,) event, launch, event groups queued before one sync,
-        # so the events bracket the kernel and not the host's launch latency
+        # the GPU first sleeps ~20 ms while the host queues all 20 (flush,)
+        # event, launch, event groups, so each pair of events brackets the
+        # GPU's own work and never the host's submission latency
         pairs = []
         with torch.cuda.stream(stream):
+            torch.cuda._sleep(40_000_000)
             for _ in range(20):
                 if flushed:
                     flush.zero_()
@@ -408,6 +411,91 @@ def time_sensors(scenes, steps, warmup, stream, dev):
     if not np.isfinite(h_valid.numpy()).all():
         raise RuntimeError("non-finite LiDAR valid fractions")
     return per_launch, e2e, n * (4096 * 4 + 8 + 16384)
+
+
+def time_render_extract(scenes, head, ages, mission_host, steps, warmup, stream, dev):
+    """The trainer's observation path kept on the device (the reference
+    renders on the host, src/sim/sensors.c:28-82, and copies every
+    observation row to the GPU, src/sim/c_api.c:104-112).  Each step copies
+    in, from page-locked memory, the scene records (2,432 B per aircraft:
+    what the renderers read), the rest of each observation row that the
+    simulator fills on the host (48 proprioceptive values and 2 LiDAR ages,
+    sensors.c:104-119: 200 B) and the mission rows (40 B); renders LiDAR
+    (with its valid fractions) and cameras straight into device observation
+    rows and camera buffers (tb_cuda_render_sensors_device, all sensors of
+    every aircraft every step); extracts the 142 features
+    (tb_cuda_extract_features_device); and copies only the features (568 B)
+    back.  Host wall clock per step, after `warmup` steps.  Returns the
+    timing and the final step's features."""
+    import torch
+
+    from turbinator_c_b200.sensors import tb_cuda_render_sensors_device as render
+
+    n = len(scenes)
+    h_scenes = torch.from_numpy(scenes.view(np.uint8).reshape(-1).copy()).pin_memory()
+    h_head = torch.from_numpy(np.ascontiguousarray(np.concatenate([head, ages], axis=1))).pin_memory()
+    h_mis = torch.from_numpy(np.ascontiguousarray(mission_host)).pin_memory()
+    h_out = torch.empty((n, tb.FEATURE_DIM), dtype=torch.float32, pin_memory=True)
+    d_scenes = torch.empty_like(h_scenes, device=dev)
+    d_head = torch.empty_like(h_head, device=dev)
+    d_mis = torch.empty_like(h_mis, device=dev)
+    d_obs = torch.zeros((n, tb.OBS_DIM), dtype=torch.float32, device=dev)
+    d_cams = torch.empty((n, tb.CAMERA_BYTES), dtype=torch.uint8, device=dev)
+    d_out = torch.empty((n, tb.FEATURE_DIM), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize(dev)
+
+    def step():
+        with torch.cuda.stream(stream):
+            d_scenes.copy_(h_scenes, non_blocking=True)
+            d_head.copy_(h_head, non_blocking=True)
+            d_mis.copy_(h_mis, non_blocking=True)
+            d_obs[:, :48].copy_(d_head[:, :48])
+            d_obs[:, 4144:4146].copy_(d_head[:, 48:50])
+            if render(d_scenes, n, d_obs.data_ptr() + 48 * 4, tb.OBS_DIM, d_obs.data_ptr() + 4146 * 4, tb.OBS_DIM,
+                      d_cams, None, stream) != 1:
+                raise RuntimeError("sensor rendering launch failed")
+            if tb.tb_cuda_extract_features_device(d_obs, d_mis, d_cams, d_out, n, stream) != 1:
+                raise RuntimeError("feature launch failed")
+            h_out.copy_(d_out, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(max(warmup, 3)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    per_step = (time.perf_counter() - t0) / steps
+    if tb.tb_cuda_synchronize(stream.cuda_stream) != 1:
+        raise RuntimeError("feature kernel reported a pipeline timeout (render leg)")
+    out = h_out.numpy().copy()
+    del d_scenes, d_head, d_mis, d_obs, d_cams, d_out
+    torch.cuda.empty_cache()
+    return per_step, out, n * (2432 + 200 + 40), n * tb.FEATURE_DIM * 4
+
+
+def render_extract_reference(scenes, head, ages, mission_host, threads):
+    """The reference's own CPU path for the same aircraft: its simulator's
+    renderers (oracle/_ref) fill the observation rows and camera bytes, then
+    tb_train_extract_features_cpu.  Returns (features, seconds rendering,
+    seconds extracting) on `threads` host threads."""
+    import oracle  # test infrastructure: the checker and the CPU baseline only
+
+    n = len(scenes)
+    t0 = time.perf_counter()
+    if oracle.have_reference_sensors():
+        lidar, valid, cams, _ = oracle.render_sensors_reference(scenes, threads=threads)
+    else:  # the restatement, pinned bit for bit to the reference renderers
+        lidar, valid, cams, _ = oracle.render_sensors_port(scenes)
+    t_render = time.perf_counter() - t0
+    obs = np.zeros((n, tb.OBS_DIM), np.float32)
+    obs[:, :48] = head
+    obs[:, 48:4144] = lidar
+    obs[:, 4144:4146] = ages
+    obs[:, 4146:4148] = valid
+    out = np.empty((n, tb.FEATURE_DIM), np.float32)
+    timed = oracle.timed_reference if oracle.have_reference() else oracle.timed_port
+    t_feat = timed(obs, np.ascontiguousarray(mission_host), cams, out, threads)
+    return out, t_render, t_feat
 
 
 def time_sensors_reference_cpu(scenes, target_s: float):
@@ -841,6 +929,28 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                            "every course scene and 64 balls in every arena scene",
                    **legs, "launches": sum(v["launches"] for v in legs.values())}
 
+    # ---- observations kept on the device: scenes in, render -> extract, features out
+    render_leg = render_check = None
+    if not args.no_sensors:
+        from turbinator_c_b200.sensors import synthetic_scenes
+
+        r_scenes = synthetic_scenes(SEED * 1000 + 500 + rank, count, balls="flight")
+        r_steps = max(1, min(args.steps, 10))
+        r_per, r_feats, r_h2d, r_d2h = time_render_extract(r_scenes, obs[:, :48], obs[:, 4144:4146], mission,
+                                                           r_steps, args.warmup, stream, dev)
+        r_max = max_over_ranks(r_per)
+        render_leg = {"value": total / r_max, "unit": UNIT, "ms_per_step": r_max * 1e3, "steps": r_steps,
+                      "h2d_bytes_per_step": r_h2d, "d2h_bytes_per_step": r_d2h,
+                      "api": "per step: scene records + 48 proprioceptive values + 2 LiDAR ages + mission copied "
+                             "in from page-locked memory, tb_cuda_render_sensors_device into device observation "
+                             "rows and cameras, tb_cuda_extract_features_device, features copied back (host wall "
+                             "clock, max over ranks)",
+                      "data": "synthetic flight-mix scenes (uniform over the 28 scenarios) with the benchmark "
+                              "batch's proprioceptive values and missions; every sensor of every aircraft "
+                              "rendered every step",
+                      "launches": 2 * (r_steps + max(args.warmup, 3))}
+        render_check = (r_scenes, r_feats)
+
     # ---- config 1 latency (1,024 aircraft)
     config1 = time_config1(stream, dev) if rank == 0 else None
 
@@ -924,6 +1034,20 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         dev, stream, rank, world, obs, mission, cams, out_timed, out_host, first, count, total,
         gatherer, gen_threads)
     gatherer.close()
+    if render_leg is not None and parity is not None:
+        from tests.parity import mismatch_counts
+
+        r_scenes, r_feats = render_check
+        idx = np.unique(np.r_[np.arange(0, count, 97), count - 1])
+        ref, _, _ = render_extract_reference(r_scenes[idx], obs[idx, :48], obs[idx, 4144:4146], mission[idx],
+                                             gen_threads)
+        e, l = mismatch_counts(r_feats[idx], ref)
+        checked, bad = sum_over_ranks([len(idx), e + l])
+        parity["render_extract_checked"], parity["render_extract_mismatches"] = checked, bad
+        parity["all_mismatches"] += bad
+        render_leg["parity"] = {"checked": checked, "mismatches": bad,
+                                "against": "the reference simulator's renderers then tb_train_extract_features_cpu "
+                                           "(oracle/_ref), every 97th aircraft"}
 
     clk = clocks.summary()
     clocks.close()
@@ -976,14 +1100,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "gpu_launches": (args.steps + e2e_steps * chunks + (onboard["launches"] if onboard else 0) +
                          (f32cam["launches"] if f32cam else 0) + (actor["launches"] if actor else 0) +
                          (sensors["launches"] if sensors else 0) + (config1["launches"] if config1 else 0) +
-                         reps),
+                         reps + (render_leg["launches"] if render_leg else 0)),
         "gpu_launches_detail": {"value_region": args.steps, "e2e_region": e2e_steps * chunks,
                                 "onboard_regions": onboard["launches"] if onboard else 0,
                                 "f32cam_region": f32cam["launches"] if f32cam else 0,
                                 "actor_inputs_region": actor["launches"] if actor else 0,
                                 "sensors_regions": sensors["launches"] if sensors else 0,
                                 "config1_region": config1["launches"] if config1 else 0,
-                                "config3_e2e_region": reps},
+                                "config3_e2e_region": reps,
+                                "render_extract_region": render_leg["launches"] if render_leg else 0},
         "clocks": clk,
     }
     if f32cam is not None:
@@ -1003,8 +1128,23 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         line["host_to_device"] = h2d
     if parity is not None:
         line["parity"] = parity
+    if render_leg is not None:
+        line["render_extract"] = render_leg
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = time_reference_cpu(obs, mission, cams, args.cpu_seconds)
+        if render_leg is not None:
+            import oracle  # test infrastructure: the CPU baseline only
+
+            if oracle.have_reference_sensors():
+                threads = host_threads()
+                k = min(count, threads * 256)
+                r_scenes = render_check[0]
+                _, t_r, t_f = render_extract_reference(r_scenes[:k], obs[:k, :48], obs[:k, 4144:4146],
+                                                       mission[:k], threads)
+                render_leg["cpu_baseline"] = {
+                    "value": k / (t_r + t_f), "unit": UNIT, "cores": threads, "kind": "reference",
+                    "sample": f"first {k} aircraft: the reference simulator's renderers ({t_r:.2f} s) then "
+                              f"tb_train_extract_features_cpu ({t_f:.2f} s), oracle/_ref, {threads} threads"}
         if onboard is not None:
             onboard["cpu_baseline"] = time_onboard_reference_cpu(obs, mission, args.cpu_seconds / 2)
         if sensors is not None:

@@ -447,6 +447,67 @@ __global__ void __launch_bounds__(kConsumerWarps * 32) features_flat_kernel(cons
     if (t < 62) f[t] = scalar;
 }
 
+/* Hybrid flat kernel: one 256-thread CTA per aircraft; thread 0 bulk-copies
+ * the aircraft's 16 KB camera block into shared memory (completion counted on
+ * an mbarrier, bounded wait) while every warp loads its LiDAR rows straight
+ * into registers with 128-bit streaming loads.  16 KB of shared memory and at
+ * most 32 registers a thread let 8 CTAs share an SM, so up to 8 x SMs
+ * aircraft -- all of BASELINE config 1 -- are in flight at once, every byte
+ * requested in the first wave. */
+constexpr int kHybridThreads = kConsumerWarps * 32;
+__global__ void __launch_bounds__(kHybridThreads, 8) features_hybrid_kernel(const float *__restrict__ obs,
+                                                                           const float *__restrict__ mission,
+                                                                           const unsigned char *__restrict__ cameras,
+                                                                           float *__restrict__ features,
+                                                                           unsigned long long wait_ns,
+                                                                           unsigned int *__restrict__ status) {
+    __shared__ __align__(128) unsigned char cam[kCameraBytes];
+    __shared__ __align__(8) unsigned long long bar;
+    const unsigned long long sample = blockIdx.x;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t bar_addr = smem_addr(&bar);
+    if (threadIdx.x == 0) {
+        mbar_init(bar_addr, 1);
+        fence_mbar_init();
+        if (cameras) {
+            mbar_arrive_expect_tx(bar_addr, kCameraBytes);
+            bulk_load(smem_addr(cam), cameras + sample * kCameraBytes, kCameraBytes, bar_addr, evict_first_policy());
+        }
+    }
+    const int head = warp >> 2, el_sector = warp & 3; /* LiDAR rows 4w..4w+3 */
+    const float *o = obs + sample * kObsDim;
+    const float4 *rows = reinterpret_cast<const float4 *>(o + kLidarOffset) + (head * 16 + el_sector * 4) * 32 + lane;
+    const float4 r0 = __ldcs(rows), r1 = __ldcs(rows + 32), r2 = __ldcs(rows + 64), r3 = __ldcs(rows + 96);
+    const int t = warp * 32 + lane;
+    float *f = features + sample * kFeatureDim;
+    if (t < 62) f[t] = scalar_feature(t, o, mission + sample * kMissionDim);
+    float sum;
+    int counts;
+    lidar_band(r0, r1, r2, r3, sum, counts);
+    if ((lane & 3) == 0) f[62 + head * 32 + el_sector * 8 + (lane >> 2)] = lidar_sector_mean(sum, counts);
+
+    __syncthreads(); /* the barrier is initialised before anyone waits on it */
+    uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0, c2 = c0, c3 = c0;
+    if (cameras) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_addr, 0, wait_ns))) {
+            /* the copy did not land in time: report it, and wait (bounded
+             * again) so that no copy lands in a retired CTA's shared memory */
+            if (lane == 0) atomicOr(status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
+            if (threadIdx.x == 0) mbar_wait(bar_addr, 0, wait_ns);
+            return;
+        }
+        const int camera = warp >> 1, qy = warp & 1; /* camera half-image w */
+        const uint4 *half = reinterpret_cast<const uint4 *>(cam) + camera * 256 + qy * 128 + lane;
+        c0 = half[0];
+        c1 = half[32];
+        c2 = half[64];
+        c3 = half[96];
+    }
+    const uint32_t bytes = quadrant_bytes(c0, c1, c2, c3);
+    if (lane == 0 || lane == 2) f[126 + (warp >> 1) * 4 + (warp & 1) * 2 + (lane >> 1)] = camera_feature(bytes);
+}
+
 /* ------------------------------------------------------------------ */
 /* Direct kernel for rows that are not 16-byte aligned: one warp per
  * aircraft, plain loads, same arithmetic. */
@@ -544,6 +605,9 @@ cudaError_t device_info(int dev, const DeviceInfo **out) {
         cudaError_t st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (st == cudaSuccess) st = staged_occupancy<false>(&b8);
         if (st == cudaSuccess) st = staged_occupancy<true>(&b32);
+        if (st == cudaSuccess) /* shared memory for 8 hybrid CTAs of 16 KB per SM */
+            st = cudaFuncSetAttribute(features_hybrid_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      cudaSharedmemCarveoutMaxShared);
         if (st != cudaSuccess) return st;
         d.sms = sms;
         d.blocks_per_sm[0] = b8;
@@ -595,7 +659,16 @@ static int launch_features(const float *obs, const float *mission, const void *c
                                         static_cast<unsigned long long>(info->sms);
     const bool flat = !kF32Cam && aligned_rows && !limited_grid && flat_choice >= 0 &&
                       (flat_choice > 0 || batch <= flat_max);
-    if (flat) {
+    if (flat && flat_choice == 2) {
+        unsigned int *status = tb_status_slot(stream);
+        if (!status) {
+            if (launch_error) *launch_error = static_cast<int>(cudaErrorInvalidDevice);
+            return 0;
+        }
+        features_hybrid_kernel<<<static_cast<unsigned int>(batch), kHybridThreads, 0, s>>>(
+            obs, mission, static_cast<const unsigned char *>(cameras), features,
+            (opts && opts->wait_ns) ? opts->wait_ns : kDefaultWaitNs, status);
+    } else if (flat) {
         features_flat_kernel<<<static_cast<unsigned int>(batch), kConsumerWarps * 32, 0, s>>>(
             obs, mission, static_cast<const unsigned char *>(cameras), features);
     } else if (aligned_rows) {
