@@ -150,3 +150,30 @@ def test_faster_than_the_reference_kernels():
     ref = timed(lambda: oracle._ref_actor.tb_ref_actor_inputs(*ptrs, n))
     print(f"\nactor inputs, 65,536 aircraft: this library {mine:.3f} ms, reference kernels {ref:.3f} ms")
     assert mine < ref
+
+
+@pytest.mark.skipif(not oracle.have_reference_actor_inputs(), reason="reference GPU build absent")
+@pytest.mark.parametrize("config", [1, 2, 4])
+def test_onboard_deviation_from_the_reference_gpu_evaluation(config):
+    """The onboard values against the reference's own GPU evaluation of
+    onboard_features.cuh (its learner's tactical/prior slots, computed with
+    CUDA's float transcendentals), per BASELINE configuration: every value
+    within the reference test's 5e-5, flags identical; the counts outside the
+    north-star bar 1e-6 + 1e-5*|ref| are printed (recorded in the design
+    notes)."""
+    seed, n, stress = tb.CONFIGS[config]
+    obs, mission, cams, _ = tb.generate(seed, 0, n, stress=stress)
+    d, (proprio, mvec, tac, pri, lidar, luma) = run(obs, mission, cams)
+    ref_outs = _outputs(n)
+    oracle.actor_inputs_reference_gpu(*d, ref_outs, n)
+    rt, rpri = ref_outs[2].cpu().numpy(), ref_outs[3].cpu().numpy()
+    mine = np.concatenate([tac, pri], 1).astype(np.float64)
+    theirs = np.concatenate([rt, rpri], 1).astype(np.float64)
+    dev = np.abs(mine - theirs)
+    over = dev > 1e-6 + 1e-5 * np.abs(theirs)
+    r, c = np.unravel_index(np.argmax(dev), dev.shape)
+    flags = sum(int(np.count_nonzero(mine[:, f] != theirs[:, f])) for f in FLAGS_TACTICAL + (24 + 14,))
+    print(f"\nconfig {config} against the reference GPU evaluation: {int(over.sum())} values outside the bar "
+          f"({int(over.any(axis=1).sum())} of {n} aircraft), worst {dev.max():.3g} at output {c}, "
+          f"{flags} flags differing")
+    assert dev.max() <= 5e-5 and flags == 0

@@ -1,0 +1,101 @@
+"""The sensor kernel's float decisions (turbinator_c_b200/csrc/sensors_kernel.cu:
+certain_miss and the camera ground test in trace) restated with numpy float32
+arithmetic and checked against the double arithmetic they stand in for, on
+cases built to sit at the decision boundaries: rays tangent to a sphere within
+a relative 1e-12 .. 1e-3, spheres from 1 mm to 1e6 m away, and ground rays
+grazing the 0.05 m and sky-distance limits.  A float decision may decline to
+decide; it must never decide differently from the double arithmetic.
+
+float32 FMA is emulated as one float64 operation rounded to float32 (the
+product of two float32 values is exact in float64); the rare double rounding
+this allows is far inside the margins under test.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+F32 = np.float32
+
+
+def fma32(a, b, c):
+    return (a.astype(np.float64) * b.astype(np.float64) + c.astype(np.float64)).astype(F32)
+
+
+def certain_miss(oc, rr, d):
+    """The kernel's test: True where the float discriminant is below -margin."""
+    occ = oc[:, 0] * oc[:, 0] + oc[:, 1] * oc[:, 1] + oc[:, 2] * oc[:, 2]
+    f = oc.astype(F32)
+    df = d.astype(F32)
+    c = (rr - occ).astype(F32)
+    margin = (2.0 ** -18 * (occ + rr)).astype(F32)
+    b = fma32(f[:, 2], df[:, 2], fma32(f[:, 1], df[:, 1], f[:, 0] * df[:, 0]))
+    return fma32(b, b, c) < -margin
+
+
+def double_disc(oc, rr, d):
+    """sphere_hit's discriminant, in the simulator's order."""
+    occ = oc[:, 0] * oc[:, 0] + oc[:, 1] * oc[:, 1] + oc[:, 2] * oc[:, 2]
+    b = oc[:, 0] * d[:, 0] + oc[:, 1] * d[:, 1] + oc[:, 2] * d[:, 2]
+    return b * b - occ + rr
+
+
+def unit(v):
+    return v / np.linalg.norm(v, axis=1, keepdims=True)
+
+
+def tangent_cases(rng, n):
+    """Rays from the origin passing the sphere centre c at distance r (1 + eps)."""
+    dist = 10.0 ** rng.uniform(-3, 6, n)
+    r = dist * 10.0 ** rng.uniform(-4, -0.05, n)
+    c = unit(rng.normal(size=(n, 3))) * dist[:, None]
+    eps = rng.choice([-1, 1], n) * 10.0 ** rng.uniform(-12, -3, n)
+    miss = r * (1 + eps)                              # closest approach
+    ang = np.arcsin(np.clip(miss / dist, -1, 1))
+    axis = unit(c)
+    perp = unit(np.cross(axis, rng.normal(size=(n, 3))))
+    d = unit(axis * np.cos(ang)[:, None] + perp * np.sin(ang)[:, None])
+    return -c, r * r, d                               # oc = origin - centre
+
+
+def test_float_miss_test_never_contradicts_the_double_discriminant():
+    rng = np.random.default_rng(20261202)
+    decided = 0
+    for _ in range(20):
+        oc, rr, d = tangent_cases(rng, 200_000)
+        miss = certain_miss(oc, rr, d)
+        disc = double_disc(oc, rr, d)
+        bad = miss & (disc >= 0)
+        assert not bad.any(), f"{bad.sum()} float misses with a double discriminant >= 0"
+        decided += int(miss.sum())
+    # wide random rays: almost every one is ruled out in float
+    oc = rng.normal(size=(200_000, 3)) * 10.0 ** rng.uniform(-1, 4, (200_000, 1))
+    rr = (np.linalg.norm(oc, axis=1) * 10.0 ** rng.uniform(-3, -1, 200_000)) ** 2
+    d = unit(rng.normal(size=(200_000, 3)))
+    miss = certain_miss(oc, rr, d)
+    assert not (miss & (double_disc(oc, rr, d) >= 0)).any()
+    assert miss.mean() > 0.95 and decided > 50_000   # both outcomes occur near tangency too
+
+
+def ground_decision(oz, dz, best):
+    """The kernel's float ground test: 1 certain hit, 0 certain miss, -1 undecided."""
+    tf = (-(oz.astype(F32)) / dz.astype(F32)).astype(np.float64)
+    hit = (tf > 0.05 * (1 + 1e-6)) & (tf < best * (1 - 1e-6))
+    miss = (tf < 0.05 * (1 - 1e-6)) | (tf > best * (1 + 1e-6))
+    return np.where(hit, 1, np.where(miss, 0, -1))
+
+
+def test_float_ground_test_never_contradicts_the_double_division():
+    rng = np.random.default_rng(7)
+    n = 2_000_000
+    dz = -(10.0 ** rng.uniform(-5, 0, n))
+    best = rng.choice([30.0, 120.0, 300.0, 1e4], n)
+    # heights that put t = -oz/dz near 0.05, near best, and anywhere
+    target = np.where(rng.uniform(size=n) < 0.4, 0.05, np.where(rng.uniform(size=n) < 0.6, best, 0.0))
+    t_want = np.where(target > 0, target * (1 + rng.choice([-1, 1], n) * 10.0 ** rng.uniform(-12, -4, n)),
+                      10.0 ** rng.uniform(-3, 5, n))
+    oz = -t_want * dz
+    t = (0 - oz) / dz
+    exact = (t > 0.05) & (t < best)
+    dec = ground_decision(oz, dz, best)
+    assert not ((dec == 1) & ~exact).any() and not ((dec == 0) & exact).any()
+    assert (dec >= 0).mean() > 0.3                    # most cases sit at a limit on purpose

@@ -231,3 +231,23 @@ def test_full_batch_sampled_and_deterministic():
     sel = torch.from_numpy(pick).to(DEV)
     got = tuple(t.index_select(0, sel).cpu().numpy() for t in outs[0]) + (None,)
     assert_same(got, oracle.render_sensors_reference(scenes[pick]), "65536 sample")
+
+
+def test_expf_error_bound_used_by_the_float_fog(tmp_path):
+    """The sensor kernel's float fog (sensors_kernel.cu: shade) relies on
+    CUDA's __expf being within 3e-7 (absolute) of exp for every argument
+    a <= 0.  Checked on every float in [-88, 0] against CUDA's double exp
+    (below -88 both are under 1e-38)."""
+    import subprocess
+
+    src = os.path.join(os.path.dirname(os.path.abspath(__file__)), "expf_bound.cu")
+    exe = str(tmp_path / "expf_bound")
+    nvcc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+    subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-o", exe, src], check=True,
+                   timeout=300)
+    run = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert run.returncode == 0, run.stderr
+    worst, where, count = run.stdout.split()
+    print(f"\n__expf: largest |error| {float(worst):.3e} at a = {float(where):.9g} over {int(count)} arguments")
+    assert int(count) > 1_000_000_000
+    assert float(worst) <= 3e-7

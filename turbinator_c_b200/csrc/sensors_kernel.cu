@@ -123,6 +123,7 @@ struct UnitHead {
     int dome;                        /* the dome can be hit before the sky distance */
     int cull;                        /* the attitude is a rotation: culling allowed */
     int shelf;                       /* scenario 10's raised ground at z = 9, x >= 20 */
+    int float_ground;                /* camera rays may keep the ground distance in float */
 };
 
 /* One unit's scene, prepared for tracing from one origin. */
@@ -130,6 +131,8 @@ struct UnitScene {
     double2 oc_xy[kMaxSpheres]; /* origin - centre, x y */
     double2 oc_zq[kMaxSpheres]; /* origin - centre z, |origin - centre|^2 */
     double rr[kMaxSpheres];     /* radius^2 */
+    float4 f_oc[kMaxSpheres];   /* float copies for the miss test: origin - centre, rr - |oc|^2 */
+    float f_margin[kMaxSpheres]; /* the miss test's error margin (+inf: no float test) */
     UnitHead h;
     int kept_obstacles, kept_opponent, kept_total; /* the unit's list, in trace order */
     unsigned int keep_mask[kSphereWarps], obst_mask[kSphereWarps], opp_mask[kSphereWarps];
@@ -159,20 +162,68 @@ __device__ __forceinline__ double sphere_hit(const UnitScene &s, int i, Vec d, d
     return t > 0.05 ? t : INFINITY;
 }
 
+/* True when sphere_hit would certainly find disc < 0 for ray d (no hit):
+ * the discriminant evaluated in float from float copies of d and of the
+ * sphere's terms lies below minus its error margin.  Error bound, with
+ * u = 2^-24, L^2 = |oc|^2 and a unit ray (|d| <= 1 + 1e-8, which holds
+ * whenever the unit's attitude passes the culling test; other units get an
+ * infinite margin): rounding oc and d to float and forming b = oc.d with one
+ * product and two FMAs puts b within 5.02 u L of oc.d; b*b is then within
+ * 10.05 u L^2; rr - |oc|^2 rounded once to float adds u (|oc|^2 + rr); the
+ * final FMA adds u (2 L^2 + rr).  So |disc_float - disc_exact| <= (13.1 L^2
+ * + 2.01 rr) u < 2^-20 (L^2 + rr), while the double discriminant is within
+ * 2^-51 (2 L^2 + rr) of disc_exact.  The margin stored is 2^-18 (L^2 + rr),
+ * four times the float bound, so disc_float < -margin proves the double
+ * disc < 0.  NaN fails the comparison and takes the double test. */
+__device__ __forceinline__ bool certain_miss(const UnitScene &s, int i, float dx, float dy, float dz) {
+    const float4 o = s.f_oc[i];
+    const float b = __fmaf_rn(o.z, dz, __fmaf_rn(o.y, dy, __fmul_rn(o.x, dx)));
+    return __fmaf_rn(b, b, o.w) < -s.f_margin[i];
+}
+
+/* The ground-plane distance t = (0 - oz) / d.z as the simulator computes it. */
+__device__ __forceinline__ double ground_distance(const UnitScene &s, Vec d) { return (0 - s.h.origin[2]) / d.z; }
+
 /* trace (sensors.c:11-26): nearest hit along d from the unit's origin, in the
  * simulator's test order (ground, shelf, obstacles, opponent, dome, balls);
- * kind -1 sky, 0 ground, 1 obstacle, 2 opponent, 3 dome, 4 ball. */
-__device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
+ * kind -1 sky, 0 ground, 1 obstacle, 2 opponent, 3 dome, 4 ball.  Spheres
+ * that certainly miss are skipped by the float test above.  For camera rays
+ * (kCamera) of units with a unit attitude and no shelf, the ground test is
+ * first decided in float: t_f = -oz_f / dz_f is within 4 u of the double t,
+ * so t > 0.05 and t < best are certain (or certainly false) when t_f clears
+ * them by a relative 1e-6.  A certain ground hit keeps t_f and leaves
+ * `exact` false; the double division is made as soon as anything needs the
+ * exact distance (a sphere the float test cannot rule out, the dome) and by
+ * the caller if the shading needs it.  A ground hit too close to call takes
+ * the double division at once. */
+template <bool kCamera>
+__device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind, bool &exact) {
     double best = s.h.best0;
     kind = -1;
+    exact = true;
     const double ox = s.h.origin[0], oy = s.h.origin[1], oz = s.h.origin[2];
+    const float dxf = __double2float_rn(d.x), dyf = __double2float_rn(d.y), dzf = __double2float_rn(d.z);
     if (d.z < -1e-5) {
-        const double t = (0 - oz) / d.z;
-        if (t > 0.05 && t < best) {
-            best = t;
-            kind = 0;
+        bool decided = false;
+        if (kCamera && s.h.float_ground) {
+            const double tf = static_cast<double>(__fdiv_rn(-__double2float_rn(oz), dzf));
+            if (tf > 0.05 * (1 + 1e-6) && tf < best * (1 - 1e-6)) {
+                best = tf;
+                kind = 0;
+                exact = false;
+                decided = true;
+            } else if (tf < 0.05 * (1 - 1e-6) || tf > best * (1 + 1e-6)) {
+                decided = true;
+            }
         }
-        if (s.h.shelf) {
+        if (!decided) {
+            const double t = (0 - oz) / d.z;
+            if (t > 0.05 && t < best) {
+                best = t;
+                kind = 0;
+            }
+        }
+        if (s.h.shelf) { /* float_ground is off in shelf scenes: best is exact here */
             const double t2 = (9 - oz) / d.z;
             if (t2 > 0.05 && t2 < best && ox + t2 * d.x >= 20) {
                 best = t2;
@@ -182,6 +233,11 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
     }
     int i = 0;
     for (; i < s.kept_obstacles; ++i) {
+        if (certain_miss(s, i, dxf, dyf, dzf)) continue;
+        if (kCamera && !exact) {
+            best = ground_distance(s, d);
+            exact = true;
+        }
         const double t = sphere_hit(s, i, d, best);
         if (t < best) {
             best = t;
@@ -190,14 +246,24 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
     }
     if (s.h.arena) {
         if (s.kept_opponent) {
-            const double t = sphere_hit(s, i, d, best);
-            if (t < best) {
-                best = t;
-                kind = 2;
+            if (!certain_miss(s, i, dxf, dyf, dzf)) {
+                if (kCamera && !exact) {
+                    best = ground_distance(s, d);
+                    exact = true;
+                }
+                const double t = sphere_hit(s, i, d, best);
+                if (t < best) {
+                    best = t;
+                    kind = 2;
+                }
             }
             ++i;
         }
         if (s.h.dome) {
+            if (kCamera && !exact) {
+                best = ground_distance(s, d);
+                exact = true;
+            }
             const double a = d.x * d.x + d.y * d.y, b = 2 * (ox * d.x + oy * d.y);
             const double disc = b * b - 4 * a * s.h.dome_cc;
             if (a > 1e-9 && disc >= 0) {
@@ -210,6 +276,11 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
         }
     }
     for (; i < s.kept_total; ++i) {
+        if (certain_miss(s, i, dxf, dyf, dzf)) continue;
+        if (kCamera && !exact) {
+            best = ground_distance(s, d);
+            exact = true;
+        }
         const double t = sphere_hit(s, i, d, best);
         if (t < best) {
             best = t;
@@ -222,14 +293,41 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
 /* shade()'s distance factor, sensors.c:66. */
 __device__ __forceinline__ double fog(double distance) { return 0.75 + 0.25 * exp(-distance / 80); }
 
-/* shade (sensors.c:59-68); the sky's factor comes precomputed. */
-__device__ __forceinline__ uint32_t shade(const UnitScene &s, double distance, int kind, double dz) {
+/* Distance from a half-integer beyond which the float-fog byte below is
+ * certain (three times the error bound derived at shade). */
+constexpr float kFogMargin = 3e-4f;
+
+/* shade (sensors.c:59-68); the sky's factor comes precomputed.  A hit's
+ * byte round(luma * fog(d) * 255) is first formed in float with __expf: the
+ * argument -d/80 in float is within 6.3 u of -d/80 (d itself within 4 u when
+ * it is trace's float ground distance), which moves exp by at most
+ * 6.3 u / e; __expf adds at most 3e-7 absolute for arguments <= 0 (checked
+ * on every float argument in [-88, 0] by tests/test_sensors_gpu.py); the FMA
+ * and two products add 4 u relative.  luma <= 1 and fog <= 1, so the float
+ * value x = luma * fog * 255 is within 255 (0.25 * 3.1e-7 + 2.4e-7) < 1e-4
+ * of the double expression, which is itself within 2e-13 of the exact value;
+ * adding 0.5 rounds by at most 7.6e-6.  When x + 0.5 lies more than
+ * kFogMargin from an integer, the double expression rounds (half away from
+ * zero, x >= 0) to the same integer.  Otherwise -- about 0.06 % of pixels --
+ * the double expression is evaluated, with the exact ground distance when
+ * trace kept a float one (`exact` false, kind 0). */
+__device__ __forceinline__ uint32_t shade(const UnitScene &s, double distance, int kind, Vec d, bool exact) {
+    const double dz = d.z;
     double luma = 0.22 + 0.15 * fmax(-1.0, fmin(1.0, dz));
     if (kind == 0) luma = 0.28 + 0.17 * fmax(0.0, fmin(1.0, -dz));
     if (kind == 1) luma = 0.65;
     if (kind == 2) luma = 0.90;
     if (kind == 3) luma = 0.46;
     if (kind == 4) luma = 1.0;
+    if (kind >= 0 && distance < 1e30) {
+        const float e = __expf(__fmul_rn(-__double2float_rn(distance), 0.0125f));
+        const float x = __fmul_rn(__fmul_rn(__double2float_rn(luma), __fmaf_rn(0.25f, e, 0.75f)), 255.0f);
+        const float y = __fadd_rn(x, 0.5f);
+        const float k = floorf(y);
+        const float r = y - k;
+        if (r > kFogMargin && r < 1.0f - kFogMargin) return static_cast<uint32_t>(fminf(255.0f, fmaxf(0.0f, k)));
+    }
+    if (!exact) distance = ground_distance(s, d);
     luma *= kind < 0 ? s.h.sky_fog : fog(distance);
     return static_cast<uint32_t>(fmax(0.0, fmin(255.0, round(luma * 255))));
 }
@@ -305,6 +403,7 @@ __device__ __forceinline__ void unit_head(UnitHead &h, const tb_sensor_scene *__
     const double rho = sqrt(ox * ox + oy * oy);
     h.dome = !(h.cull && dome - rho > h.best0 * (1 + 1e-9) + 1e-9);
     h.shelf = scenario == 10;
+    h.float_ground = h.cull && !h.shelf && fabs(oz) < 1e30;
     h.arena = arena;
     h.n_obstacles = min(max(scene->obstacle_count, 0), TB_SENSOR_MAX_OBSTACLES);
     h.n_balls = min(max(scene->ball_count, 0), TB_SENSOR_MAX_BALLS);
@@ -319,7 +418,7 @@ __device__ __forceinline__ void unit_head(UnitHead &h, const tb_sensor_scene *__
 __device__ __forceinline__ void prepare_unit(UnitScene &s, const tb_sensor_scene *__restrict__ scene, int part) {
     const int t = threadIdx.x;
     double ocx = 0, ocy = 0, ocz = 0, occ = 0, rr = 0;
-    bool keep = false;
+    bool keep = false, float_test = false;
     int n_obst = 0, arena = 0;
     if (t < 32 * kSphereWarps) {
         UnitHead h;
@@ -358,6 +457,7 @@ __device__ __forceinline__ void prepare_unit(UnitScene &s, const tb_sensor_scene
             occ = ocx * ocx + ocy * ocy + ocz * ocz;
             rr = radius * radius;
             keep = !(h.cull && cone_misses(h, g_cone[part], cx, cy, cz, radius));
+            float_test = h.cull && occ + rr < 1e30; /* unit rays, no float overflow (NaN fails) */
         }
         const unsigned int m = __ballot_sync(0xffffffffu, keep);
         const unsigned int obst = __ballot_sync(0xffffffffu, keep && t < n_obst);
@@ -377,6 +477,9 @@ __device__ __forceinline__ void prepare_unit(UnitScene &s, const tb_sensor_scene
             s.oc_xy[pos] = make_double2(ocx, ocy);
             s.oc_zq[pos] = make_double2(ocz, occ);
             s.rr[pos] = rr;
+            s.f_oc[pos] = make_float4(__double2float_rn(ocx), __double2float_rn(ocy), __double2float_rn(ocz),
+                                      __double2float_rn(rr - occ));
+            s.f_margin[pos] = float_test ? __double2float_rn(0x1.0p-18 * (occ + rr)) : INFINITY;
         }
         if (t == 0) {
             int total = 0, kept_obst = 0, kept_opp = 0;
@@ -432,7 +535,8 @@ __global__ void __launch_bounds__(kThreads, TB_SENSOR_MIN_BLOCKS)
                 if (!(static_cast<double>(hash & 0xffff) / 65536.0 < 0.005 || blocked)) {
                     const Vec rw = rotate(qw, qx, qy, qz, Vec{g_lidar_x[bin], g_lidar_y[bin], g_lidar_z[bin]});
                     int kind;
-                    double range = trace(s, rw, kind);
+                    bool exact;
+                    double range = trace<false>(s, rw, kind, exact);
                     const double noise = (static_cast<double>((hash >> 16) & 0xffff) / 32768.0 - 1.0) * 0.02;
                     range = fmax(0.05, fmin(max_range, range + noise));
                     value = static_cast<float>(range);
@@ -464,8 +568,9 @@ __global__ void __launch_bounds__(kThreads, TB_SENSOR_MIN_BLOCKS)
                     const Vec dir = rotate(qw, qx, qy, qz,
                                            Vec{g_camera_x[pixel + j], g_camera_y[pixel + j], g_camera_z[pixel + j]});
                     int kind;
-                    const double d = trace(s, dir, kind);
-                    word |= shade(s, d, kind, dir.z) << (8 * j);
+                    bool exact;
+                    const double d = trace<true>(s, dir, kind, exact);
+                    word |= shade(s, d, kind, dir, exact) << (8 * j);
                 }
                 if (cameras)
                     *reinterpret_cast<uint32_t *>(cameras + scene_index * kCameraPixels + pixel) = word;
