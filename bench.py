@@ -46,7 +46,7 @@ UNIT = "samples/s"
 BATCH_PER_GPU = 65536
 SEED = 2
 FALLBACK_HBM_GBS = 6650.0
-PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "features_staged_kernel_traffic.txt")
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "features_flat_kernel_traffic.txt")
 SENSOR_SCENES = 32768
 SENSOR_PROFILE = os.path.join(ROOT, "profiles", "sensors_kernel_pipes.txt")
 RAYS_PER_SCENE = 4096 + 16384
@@ -1093,10 +1093,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                                   "this pool is 7,094 GB/s (profiles/hbm_patterns_b200.md)",
                      "traffic": (tps * count) if tps else None,
                      "traffic_source": "not measured in this run: DRAM bytes per aircraft of the committed ncu "
-                                       "capture (16,384 aircraft, profiles/features_staged_kernel_b16384.md) "
+                                       "capture (16,384 aircraft, profiles/features_flat_kernel_b16384.md) "
                                        "times this launch's aircraft",
                      "algorithmic_bytes_per_launch": count * tb.BYTES_PER_SAMPLE,
-                     "kernel": "features_staged_kernel", "avg_launch_ms": avg_launch_s * 1e3},
+                     "kernel": "features_flat_kernel", "avg_launch_ms": avg_launch_s * 1e3},
         "gpu_launches": (args.steps + e2e_steps * chunks + (onboard["launches"] if onboard else 0) +
                          (f32cam["launches"] if f32cam else 0) + (actor["launches"] if actor else 0) +
                          (sensors["launches"] if sensors else 0) + (config1["launches"] if config1 else 0) +

@@ -350,3 +350,21 @@ def test_pipeline_timeout_is_reported_only_on_its_own_stream():
     assert tb.tb_cuda_synchronize(stream_a) == 0      # reported to its own stream
     assert tb.tb_cuda_synchronize(stream_a) == 1      # once
     check_features(run_device(obs, mission, cams, stream=stream_a), expected, "stream A after its timeout")
+
+
+def test_host_abi_buffer_page_locked_only_at_its_start():
+    """Observation rows whose first pages are page-locked (cudaHostRegister of
+    a prefix) but the rest pageable: the handle must see the buffer as
+    pageable and still return every row correct."""
+    n = 1200
+    obs, mission, cams, _ = tb.generate(33, 0, n)
+    prefix = 64 * 4148 * 4 // 4096 * 4096
+    cudart = torch.cuda.cudart()
+    assert int(cudart.cudaHostRegister(obs.ctypes.data, prefix, 0)) == 0
+    try:
+        out = np.zeros((n, 142), np.float32)
+        with tb.FeatureBatch(0, n) as fb:
+            assert fb.extract(obs, mission, cams, n, out) == 1, fb.error()
+    finally:
+        cudart.cudaHostUnregister(obs.ctypes.data)
+    check_features(out, oracle.features(obs, mission, cams), "partly page-locked")

@@ -217,8 +217,9 @@ def launch(obs, mission, cameras, features, batch_size: int, stream=None, *,
            force_direct: bool = False, grid_limit: int = 0, wait_ns: int = 0,
            stall_sample: int = -1, flat: int = 0) -> int:
     """``tb_features_launch`` with explicit options (kernel choice, grid cap,
-    pipeline wait limit, the test-only stalled-sample hook, and the flat
-    kernel: 0 = by batch size, 1 = always, -1 = never)."""
+    pipeline wait limit, the test-only stalled-sample hook, and the u8 kernel:
+    flat >= 0 the one-CTA-per-aircraft kernel (the default), -1 the staged
+    ring kernel)."""
     opts = LaunchOpts(int(force_direct), int(grid_limit), int(wait_ns), int(stall_sample), int(flat))
     return load_library().tb_features_launch(
         _ptr(obs), _ptr(mission), _ptr(cameras), _ptr(features), batch_size,

@@ -8,7 +8,8 @@
  *  - A handle may span several GPUs (tb_cuda_feature_batch_create_multi):
  *    each call's rows are split into contiguous per-device shards.
  *  - Within a device the rows are split again into "lanes", one host thread
- *    each.  Page-locked caller buffers are copied straight to the device in
+ *    each (the caller's and workers that the handle starts on its first call
+ *    with more than one lane and keeps until it is destroyed).  Page-locked caller buffers are copied straight to the device in
  *    chunks alternating between two streams.  Large pageable calls (the
  *    trainer's calloc'd batch buffers) are copied by each lane's thread into
  *    a double-buffered page-locked staging area, so the host copy of one
@@ -71,12 +72,25 @@ typedef struct tb_device_shard {
     tb_lane lanes[TB_MAX_LANES];
 } tb_device_shard;
 
+struct tb_lane_job;
+
 struct tb_cuda_feature_batch {
     int device_id;                /* first device (the reference handle's device) */
     size_t max_batch;
     int device_count;
     tb_device_shard shards[TB_MAX_DEVICES];
     char error[192];
+    /* Worker threads that run a call's lanes beside the calling thread; started
+     * on the first call with more than one lane, kept until the handle is
+     * destroyed.  A call posts its jobs and takes part itself. */
+    int pool_ready;               /* lock and conditions initialised */
+    int pool_size;                /* workers started */
+    pthread_t pool_threads[TB_MAX_DEVICES * TB_MAX_LANES];
+    pthread_mutex_t pool_lock;
+    pthread_cond_t pool_work, pool_done;
+    struct tb_lane_job *pool_jobs;
+    int pool_job_count, pool_next, pool_finished, pool_quit;
+    unsigned long pool_generation;
 };
 
 /* ------------------------------------------------------------------ */
@@ -196,8 +210,23 @@ tb_cuda_feature_batch *tb_cuda_feature_batch_create(int device_id, size_t max_ba
     return tb_cuda_feature_batch_create_multi(&device_id, 1, max_batch);
 }
 
+static void pool_stop(tb_cuda_feature_batch *batch) {
+    if (!batch->pool_ready) return;
+    pthread_mutex_lock(&batch->pool_lock);
+    batch->pool_quit = 1;
+    pthread_cond_broadcast(&batch->pool_work);
+    pthread_mutex_unlock(&batch->pool_lock);
+    for (int i = 0; i < batch->pool_size; ++i) pthread_join(batch->pool_threads[i], NULL);
+    pthread_cond_destroy(&batch->pool_work);
+    pthread_cond_destroy(&batch->pool_done);
+    pthread_mutex_destroy(&batch->pool_lock);
+    batch->pool_ready = 0;
+    batch->pool_size = 0;
+}
+
 void tb_cuda_feature_batch_destroy(tb_cuda_feature_batch *batch) {
     if (!batch) return;
+    pool_stop(batch);
     for (int d = 0; d < batch->device_count; ++d) shard_release(&batch->shards[d]);
     cudaSetDevice(batch->device_id);
     free(batch);
@@ -207,14 +236,20 @@ const char *tb_cuda_feature_batch_error(const tb_cuda_feature_batch *batch) {
     return batch ? batch->error : "CUDA feature batch unavailable";
 }
 
-/* 1 if `p` is page-locked (or otherwise device-visible) host memory. */
-static int host_pinned(const void *p) {
+/* 1 if the byte at `p` is page-locked (or otherwise device-visible) host memory. */
+static int host_byte_pinned(const void *p) {
     struct cudaPointerAttributes attr;
     if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
     return attr.type == cudaMemoryTypeHost || attr.type == cudaMemoryTypeManaged;
+}
+
+/* 1 if the first and the last byte of [p, p + bytes) are page-locked: a buffer
+ * that is page-locked only at its start takes the staged (pageable) path. */
+static int host_pinned(const void *p, size_t bytes) {
+    return host_byte_pinned(p) && host_byte_pinned((const unsigned char *)p + bytes - 1);
 }
 
 /* ------------------------------------------------------------------ */
@@ -401,6 +436,75 @@ static void *job_main(void *arg) {
     return NULL;
 }
 
+/* Worker loop: wait for a new call's jobs, take them one at a time. */
+static void *pool_worker(void *arg) {
+    tb_cuda_feature_batch *batch = (tb_cuda_feature_batch *)arg;
+    unsigned long seen = 0;
+    pthread_mutex_lock(&batch->pool_lock);
+    for (;;) {
+        while (!batch->pool_quit && batch->pool_generation == seen)
+            pthread_cond_wait(&batch->pool_work, &batch->pool_lock);
+        if (batch->pool_quit) break;
+        seen = batch->pool_generation;
+        while (batch->pool_next < batch->pool_job_count) {
+            struct tb_lane_job *job = &batch->pool_jobs[batch->pool_next++];
+            pthread_mutex_unlock(&batch->pool_lock);
+            job_main(job);
+            pthread_mutex_lock(&batch->pool_lock);
+            if (++batch->pool_finished == batch->pool_job_count) pthread_cond_broadcast(&batch->pool_done);
+        }
+    }
+    pthread_mutex_unlock(&batch->pool_lock);
+    return NULL;
+}
+
+/* Start workers until `want` run (as many as the system gives). */
+static void pool_grow(tb_cuda_feature_batch *batch, int want) {
+    if (!batch->pool_ready) {
+        if (pthread_mutex_init(&batch->pool_lock, NULL) != 0) return;
+        if (pthread_cond_init(&batch->pool_work, NULL) != 0) {
+            pthread_mutex_destroy(&batch->pool_lock);
+            return;
+        }
+        if (pthread_cond_init(&batch->pool_done, NULL) != 0) {
+            pthread_cond_destroy(&batch->pool_work);
+            pthread_mutex_destroy(&batch->pool_lock);
+            return;
+        }
+        batch->pool_ready = 1;
+    }
+    while (batch->pool_size < want &&
+           pthread_create(&batch->pool_threads[batch->pool_size], NULL, pool_worker, batch) == 0)
+        ++batch->pool_size;
+}
+
+/* Runs every job: on the pool's workers and the calling thread together. */
+static void run_jobs(tb_cuda_feature_batch *batch, tb_lane_job *jobs, int job_count) {
+    if (job_count > 1) pool_grow(batch, job_count - 1);
+    if (job_count <= 1 || !batch->pool_ready) {
+        for (int j = 0; j < job_count; ++j) job_main(&jobs[j]);
+        return;
+    }
+    pthread_mutex_lock(&batch->pool_lock);
+    batch->pool_jobs = jobs;
+    batch->pool_job_count = job_count;
+    batch->pool_next = 0;
+    batch->pool_finished = 0;
+    ++batch->pool_generation;
+    pthread_cond_broadcast(&batch->pool_work);
+    while (batch->pool_next < job_count) {
+        tb_lane_job *job = &jobs[batch->pool_next++];
+        pthread_mutex_unlock(&batch->pool_lock);
+        job_main(job);
+        pthread_mutex_lock(&batch->pool_lock);
+        if (++batch->pool_finished == job_count) pthread_cond_broadcast(&batch->pool_done);
+    }
+    while (batch->pool_finished < job_count) pthread_cond_wait(&batch->pool_done, &batch->pool_lock);
+    batch->pool_jobs = NULL;
+    batch->pool_job_count = 0;
+    pthread_mutex_unlock(&batch->pool_lock);
+}
+
 int tb_cuda_extract_features_host(tb_cuda_feature_batch *batch, const float *obs,
                                   const float *mission, const unsigned char *cameras,
                                   size_t count, float *out_features) {
@@ -411,8 +515,10 @@ int tb_cuda_extract_features_host(tb_cuda_feature_batch *batch, const float *obs
     cudaError_t status = cudaSetDevice(batch->device_id);
     if (status != cudaSuccess) return batch_fail(batch, "select device", status);
 
-    const int direct_in = host_pinned(obs) && host_pinned(mission) && host_pinned(cameras);
-    const int direct_out = host_pinned(out_features);
+    const int direct_in = host_pinned(obs, count * TB_OBS_DIM * sizeof(float)) &&
+                          host_pinned(mission, count * TB_MISSION_DIM * sizeof(float)) &&
+                          host_pinned(cameras, count * TB_CAMERA_BYTES);
+    const int direct_out = host_pinned(out_features, count * TB_OUT_ROW_BYTES);
     tb_lane_job jobs[TB_MAX_DEVICES * TB_MAX_LANES];
     int job_count = 0;
     for (int d = 0; d < batch->device_count; ++d) {
@@ -447,17 +553,7 @@ int tb_cuda_extract_features_host(tb_cuda_feature_batch *batch, const float *obs
             job->direct_out = direct_out;
         }
     }
-    pthread_t tids[TB_MAX_DEVICES * TB_MAX_LANES];
-    int started[TB_MAX_DEVICES * TB_MAX_LANES] = {0};
-    for (int j = 1; j < job_count; ++j)
-        started[j] = pthread_create(&tids[j], NULL, job_main, &jobs[j]) == 0;
-    job_main(&jobs[0]);
-    for (int j = 1; j < job_count; ++j) {
-        if (started[j])
-            pthread_join(tids[j], NULL);
-        else
-            job_main(&jobs[j]); /* could not start a thread: run it here */
-    }
+    run_jobs(batch, jobs, job_count);
     cudaSetDevice(batch->device_id);
     for (int j = 0; j < job_count; ++j) {
         if (!jobs[j].stage) continue;

@@ -27,9 +27,9 @@ typedef struct tb_features_launch_opts {
     unsigned long long wait_ns;       /* 0: default (~1 s) limit on each pipeline wait */
     long long stall_sample;           /* test hook: >= 0 withholds that sample's copies so the
                                          bounded waits expire; -1 in normal use */
-    int flat;                         /* u8 cameras, aligned rows: 0 chooses by batch size,
-                                         1 always takes the one-CTA-per-aircraft kernel,
-                                         -1 never */
+    int flat;                         /* u8 cameras, aligned rows: >= 0 takes the
+                                         one-CTA-per-aircraft kernel (the default), -1 the
+                                         staged ring kernel */
 } tb_features_launch_opts;
 
 /* Launch on the current device; same return contract as
