@@ -336,9 +336,30 @@ def time_config1(stream, dev):
         stream.synchronize()
         return statistics.median(a.elapsed_time(b) for a, b in pairs)
 
+    def amortised_us(call, flushed, k=20):
+        # k launches (each after a flush when flushed) between one pair of
+        # events, behind a GPU sleep; per launch, minus the flushes' own time
+        def group(with_call, with_flush):
+            with torch.cuda.stream(stream):
+                torch.cuda._sleep(40_000_000)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(k):
+                    if with_flush:
+                        flush.zero_()
+                    if with_call:
+                        call()
+                b.record(stream)
+            stream.synchronize()
+            return a.elapsed_time(b) * 1e3 / k
+        both = statistics.median(group(True, flushed) for _ in range(5))
+        return both - (statistics.median(group(False, True) for _ in range(5)) if flushed else 0.0)
+
     resident, flushed, clean = device_ms(entry, False), device_ms(entry, "dirty"), device_ms(entry, "clean")
     st_resident, st_flushed = device_ms(staged, False), device_ms(staged, "dirty")
     st_clean = device_ms(staged, "clean")
+    am_resident, am_flushed = amortised_us(entry, False), amortised_us(entry, True)
+    st_am_resident, st_am_flushed = amortised_us(staged, False), amortised_us(staged, True)
     host = []
     for _ in range(20):
         t0 = time.perf_counter()
@@ -358,14 +379,20 @@ def time_config1(stream, dev):
             "launch_inclusive_us": launch_us, "value_l2_flushed": n / (flushed / 1e3), "unit": UNIT,
             "roofline_frac_l2_flushed": algo / (flushed / 1e3) / 1e9 / peak,
             "roofline_frac_l2_flushed_clean": algo / (clean / 1e3) / 1e9 / peak,
+            "amortised_us_l2_resident": am_resident, "amortised_us_l2_flushed": am_flushed,
+            "roofline_frac_amortised_l2_flushed": algo / (am_flushed / 1e6) / 1e9 / peak,
             "peak_source": f"{peak_kind} hbm_gbs",
             "staged_kernel": {"device_us_l2_resident": st_resident * 1e3, "device_us_l2_flushed": st_flushed * 1e3,
-                              "device_us_l2_flushed_clean": st_clean * 1e3},
+                              "device_us_l2_flushed_clean": st_clean * 1e3,
+                              "amortised_us_l2_resident": st_am_resident, "amortised_us_l2_flushed": st_am_flushed},
+            "amortised": "per launch over 20 launches between one event pair behind a GPU sleep (event ticks "
+                         "here are ~2 us apart, so a single-launch pair cannot resolve the kernel); flushed: each "
+                         "launch after a 256 MiB rewrite, minus the rewrites' own time; medians of 5 groups",
             "flush": "l2_flushed: a 256 MiB buffer rewritten before each launch (dirty L2); "
                      "l2_flushed_clean: rewritten, then read (clean L2 holding other data)",
             "finite": bool(expected_ok),
             "timing": "medians of 20; events around each launch; host wall clock call -> stream done",
-            "launches": 10 + 6 * 20 + 20}
+            "launches": 10 + 6 * 20 + 20 + 4 * 5 * 20}
 
 
 def time_sensors(scenes, steps, warmup, stream, dev):
