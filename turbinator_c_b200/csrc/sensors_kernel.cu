@@ -123,7 +123,6 @@ struct UnitHead {
     int dome;                        /* the dome can be hit before the sky distance */
     int cull;                        /* the attitude is a rotation: culling allowed */
     int shelf;                       /* scenario 10's raised ground at z = 9, x >= 20 */
-    int float_ground;                /* camera rays may keep the ground distance in float */
 };
 
 /* One unit's scene, prepared for tracing from one origin. */
@@ -181,49 +180,23 @@ __device__ __forceinline__ bool certain_miss(const UnitScene &s, int i, float dx
     return __fmaf_rn(b, b, o.w) < -s.f_margin[i];
 }
 
-/* The ground-plane distance t = (0 - oz) / d.z as the simulator computes it. */
-__device__ __forceinline__ double ground_distance(const UnitScene &s, Vec d) { return (0 - s.h.origin[2]) / d.z; }
-
 /* trace (sensors.c:11-26): nearest hit along d from the unit's origin, in the
  * simulator's test order (ground, shelf, obstacles, opponent, dome, balls);
  * kind -1 sky, 0 ground, 1 obstacle, 2 opponent, 3 dome, 4 ball.  Spheres
- * that certainly miss are skipped by the float test above.  For camera rays
- * (kCamera) of units with a unit attitude and no shelf, the ground test is
- * first decided in float: t_f = -oz_f / dz_f is within 4 u of the double t,
- * so t > 0.05 and t < best are certain (or certainly false) when t_f clears
- * them by a relative 1e-6.  A certain ground hit keeps t_f and leaves
- * `exact` false; the double division is made as soon as anything needs the
- * exact distance (a sphere the float test cannot rule out, the dome) and by
- * the caller if the shading needs it.  A ground hit too close to call takes
- * the double division at once. */
-template <bool kCamera>
-__device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind, bool &exact) {
+ * that certainly miss are skipped by the float test above before the double
+ * one. */
+__device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
     double best = s.h.best0;
     kind = -1;
-    exact = true;
     const double ox = s.h.origin[0], oy = s.h.origin[1], oz = s.h.origin[2];
     const float dxf = __double2float_rn(d.x), dyf = __double2float_rn(d.y), dzf = __double2float_rn(d.z);
     if (d.z < -1e-5) {
-        bool decided = false;
-        if (kCamera && s.h.float_ground) {
-            const double tf = static_cast<double>(__fdiv_rn(-__double2float_rn(oz), dzf));
-            if (tf > 0.05 * (1 + 1e-6) && tf < best * (1 - 1e-6)) {
-                best = tf;
-                kind = 0;
-                exact = false;
-                decided = true;
-            } else if (tf < 0.05 * (1 - 1e-6) || tf > best * (1 + 1e-6)) {
-                decided = true;
-            }
+        const double t = (0 - oz) / d.z;
+        if (t > 0.05 && t < best) {
+            best = t;
+            kind = 0;
         }
-        if (!decided) {
-            const double t = (0 - oz) / d.z;
-            if (t > 0.05 && t < best) {
-                best = t;
-                kind = 0;
-            }
-        }
-        if (s.h.shelf) { /* float_ground is off in shelf scenes: best is exact here */
+        if (s.h.shelf) {
             const double t2 = (9 - oz) / d.z;
             if (t2 > 0.05 && t2 < best && ox + t2 * d.x >= 20) {
                 best = t2;
@@ -234,10 +207,6 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind, bo
     int i = 0;
     for (; i < s.kept_obstacles; ++i) {
         if (certain_miss(s, i, dxf, dyf, dzf)) continue;
-        if (kCamera && !exact) {
-            best = ground_distance(s, d);
-            exact = true;
-        }
         const double t = sphere_hit(s, i, d, best);
         if (t < best) {
             best = t;
@@ -247,10 +216,6 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind, bo
     if (s.h.arena) {
         if (s.kept_opponent) {
             if (!certain_miss(s, i, dxf, dyf, dzf)) {
-                if (kCamera && !exact) {
-                    best = ground_distance(s, d);
-                    exact = true;
-                }
                 const double t = sphere_hit(s, i, d, best);
                 if (t < best) {
                     best = t;
@@ -260,10 +225,6 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind, bo
             ++i;
         }
         if (s.h.dome) {
-            if (kCamera && !exact) {
-                best = ground_distance(s, d);
-                exact = true;
-            }
             const double a = d.x * d.x + d.y * d.y, b = 2 * (ox * d.x + oy * d.y);
             const double disc = b * b - 4 * a * s.h.dome_cc;
             if (a > 1e-9 && disc >= 0) {
@@ -277,10 +238,6 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind, bo
     }
     for (; i < s.kept_total; ++i) {
         if (certain_miss(s, i, dxf, dyf, dzf)) continue;
-        if (kCamera && !exact) {
-            best = ground_distance(s, d);
-            exact = true;
-        }
         const double t = sphere_hit(s, i, d, best);
         if (t < best) {
             best = t;
@@ -298,21 +255,18 @@ __device__ __forceinline__ double fog(double distance) { return 0.75 + 0.25 * ex
 constexpr float kFogMargin = 3e-4f;
 
 /* shade (sensors.c:59-68); the sky's factor comes precomputed.  A hit's
- * byte round(luma * fog(d) * 255) is first formed in float with __expf: the
- * argument -d/80 in float is within 6.3 u of -d/80 (d itself within 4 u when
- * it is trace's float ground distance), which moves exp by at most
- * 6.3 u / e; __expf adds at most 3e-7 absolute for arguments <= 0 (checked
- * on every float argument in [-88, 0] by tests/test_sensors_gpu.py); the FMA
- * and two products add 4 u relative.  luma <= 1 and fog <= 1, so the float
- * value x = luma * fog * 255 is within 255 (0.25 * 3.1e-7 + 2.4e-7) < 1e-4
- * of the double expression, which is itself within 2e-13 of the exact value;
- * adding 0.5 rounds by at most 7.6e-6.  When x + 0.5 lies more than
- * kFogMargin from an integer, the double expression rounds (half away from
- * zero, x >= 0) to the same integer.  Otherwise -- about 0.06 % of pixels --
- * the double expression is evaluated, with the exact ground distance when
- * trace kept a float one (`exact` false, kind 0). */
-__device__ __forceinline__ uint32_t shade(const UnitScene &s, double distance, int kind, Vec d, bool exact) {
-    const double dz = d.z;
+ * byte round(luma * fog(d) * 255) is first formed in float with
+ * __expf: the argument -d/80 in float is within 2.3 u of -d/80 (u = 2^-24),
+ * which moves exp by at most 2.3 u / e; __expf adds at most 3e-7 absolute for
+ * arguments <= 0 (checked on every float argument in [-88, 0] by
+ * tests/test_sensors_gpu.py); the FMA and two products add 4 u relative.
+ * luma <= 1 and fog <= 1, so the float value x = luma * fog * 255 is within
+ * 255 (0.25 * 3.6e-7 + 2.4e-7) < 1e-4 of the double expression, which is
+ * itself within 2e-13 of the exact value; adding 0.5 rounds by at most
+ * 7.6e-6.  When x + 0.5 lies more than kFogMargin from an integer, the double
+ * expression rounds (half away from zero, x >= 0) to the same integer.
+ * Otherwise -- about 0.06 % of pixels -- the double expression is evaluated. */
+__device__ __forceinline__ uint32_t shade(const UnitScene &s, double distance, int kind, double dz) {
     double luma = 0.22 + 0.15 * fmax(-1.0, fmin(1.0, dz));
     if (kind == 0) luma = 0.28 + 0.17 * fmax(0.0, fmin(1.0, -dz));
     if (kind == 1) luma = 0.65;
@@ -327,7 +281,6 @@ __device__ __forceinline__ uint32_t shade(const UnitScene &s, double distance, i
         const float r = y - k;
         if (r > kFogMargin && r < 1.0f - kFogMargin) return static_cast<uint32_t>(fminf(255.0f, fmaxf(0.0f, k)));
     }
-    if (!exact) distance = ground_distance(s, d);
     luma *= kind < 0 ? s.h.sky_fog : fog(distance);
     return static_cast<uint32_t>(fmax(0.0, fmin(255.0, round(luma * 255))));
 }
@@ -403,7 +356,6 @@ __device__ __forceinline__ void unit_head(UnitHead &h, const tb_sensor_scene *__
     const double rho = sqrt(ox * ox + oy * oy);
     h.dome = !(h.cull && dome - rho > h.best0 * (1 + 1e-9) + 1e-9);
     h.shelf = scenario == 10;
-    h.float_ground = h.cull && !h.shelf && fabs(oz) < 1e30;
     h.arena = arena;
     h.n_obstacles = min(max(scene->obstacle_count, 0), TB_SENSOR_MAX_OBSTACLES);
     h.n_balls = min(max(scene->ball_count, 0), TB_SENSOR_MAX_BALLS);
@@ -496,6 +448,96 @@ __device__ __forceinline__ void prepare_unit(UnitScene &s, const tb_sensor_scene
     __syncthreads();
 }
 
+/* The LiDAR units (2 per scene: the heads) and the camera units (8 per
+ * scene: each view's two halves) run as two kernels, so that each keeps only
+ * its own code and registers (one kernel over all ten units spilled more and
+ * ran 6-13 % slower with the float tests). */
+constexpr int kLidarUnits = 2, kCameraUnits = 8;
+
+/* LiDAR head `part` of scene `scene_index` (sensors.c:31-49). */
+__device__ __forceinline__ void render_lidar(UnitScene &s, int part, unsigned long long scene_index, float *lidar,
+                                             unsigned long long lidar_stride, float *lidar_valid,
+                                             unsigned long long valid_stride) {
+    const int t = threadIdx.x;
+    const double qw = s.h.q[0], qx = s.h.q[1], qy = s.h.q[2], qz = s.h.q[3];
+    float *out = lidar + scene_index * lidar_stride;
+    const double max_range = s.h.max_range;
+    /* SplitMix64 state before the draw of bin b is seed + (b + 1) * golden */
+    unsigned long long state = s.h.seed + static_cast<unsigned long long>(part * kUnitRays + t + 1) * kGolden;
+    int valid = 0;
+#pragma unroll 1
+    for (int k = 0; k < kUnitRays / kThreads; ++k, state += static_cast<unsigned long long>(kThreads) * kGolden) {
+        const int bin = part * kUnitRays + k * kThreads + t;
+        const unsigned long long hash = splitmix(state);
+        const bool blocked = (g_lidar_blocked[bin >> 5] >> (bin & 31)) & 1u;
+        float value = -1.0f;
+        if (!(static_cast<double>(hash & 0xffff) / 65536.0 < 0.005 || blocked)) {
+            const Vec rw = rotate(qw, qx, qy, qz, Vec{g_lidar_x[bin], g_lidar_y[bin], g_lidar_z[bin]});
+            int kind;
+            double range = trace(s, rw, kind);
+            const double noise = (static_cast<double>((hash >> 16) & 0xffff) / 32768.0 - 1.0) * 0.02;
+            range = fmax(0.05, fmin(max_range, range + noise));
+            value = static_cast<float>(range);
+            ++valid;
+        }
+        out[bin] = value;
+    }
+    if (lidar_valid) {
+        /* the last warp to finish writes the head's valid fraction */
+        valid = __reduce_add_sync(0xffffffffu, valid);
+        if ((t & 31) == 0) {
+            atomicAdd(&s.valid_count, valid);
+            __threadfence_block();
+            if (atomicAdd(&s.warps_done, 1) == kWarps - 1)
+                lidar_valid[scene_index * valid_stride + part] =
+                    static_cast<float>(atomicAdd(&s.valid_count, 0)) / 2048;
+        }
+    }
+}
+
+/* Half of camera view (part - 2) / 2 of scene `scene_index` (sensors.c:71-79): 32 rows of 64. */
+__device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned long long scene_index,
+                                              unsigned char *cameras, unsigned char *raw) {
+    const int t = threadIdx.x;
+    const double qw = s.h.q[0], qx = s.h.q[1], qy = s.h.q[2], qz = s.h.q[3];
+    const int view = (part - 2) >> 1, half = (part - 2) & 1;
+#pragma unroll 1
+    for (int k = 0; k < kUnitRays / (4 * kThreads); ++k) {
+        const int local = half * kUnitRays + k * 4 * kThreads + 4 * t; /* pixel in the view */
+        const int pixel = view * 4096 + local;
+        uint32_t word = 0;
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+            const Vec dir = rotate(qw, qx, qy, qz,
+                                   Vec{g_camera_x[pixel + j], g_camera_y[pixel + j], g_camera_z[pixel + j]});
+            int kind;
+            const double d = trace(s, dir, kind);
+            word |= shade(s, d, kind, dir.z) << (8 * j);
+        }
+        if (cameras)
+            *reinterpret_cast<uint32_t *>(cameras + scene_index * kCameraPixels + pixel) = word;
+        if (raw) {
+            /* each pixel as a 3 x 3 block of the 192 x 192 view (sensors.c:78) */
+            const uint32_t p0 = word & 255u, p1 = (word >> 8) & 255u, p2 = (word >> 16) & 255u,
+                           p3 = word >> 24;
+            const uint32_t w0 = p0 | p0 << 8 | p0 << 16 | p1 << 24;
+            const uint32_t w1 = p1 | p1 << 8 | p2 << 16 | p2 << 24;
+            const uint32_t w2 = p2 | p3 << 8 | p3 << 16 | p3 << 24;
+            const int y = local >> 6, x = local & 63;
+            unsigned char *base = raw + scene_index * static_cast<unsigned long long>(TB_SENSOR_CAMERA_RAW_PIXELS) +
+                                  view * 36864 + 3 * x;
+#pragma unroll
+            for (int dy = 0; dy < 3; ++dy) {
+                uint32_t *row = reinterpret_cast<uint32_t *>(base + (3 * y + dy) * 192);
+                row[0] = w0;
+                row[1] = w1;
+                row[2] = w2;
+            }
+        }
+    }
+}
+
+template <bool kLidar>
 __global__ void __launch_bounds__(kThreads, TB_SENSOR_MIN_BLOCKS)
     sensors_kernel(const tb_sensor_scene *__restrict__ scenes, unsigned long long units, float *__restrict__ lidar,
                    unsigned long long lidar_stride, float *__restrict__ lidar_valid, unsigned long long valid_stride,
@@ -504,96 +546,21 @@ __global__ void __launch_bounds__(kThreads, TB_SENSOR_MIN_BLOCKS)
      * rewritten only after both barriers of the unit in between, which every
      * thread passes after it finished tracing from that slot. */
     __shared__ UnitScene slots[2];
-    const int t = threadIdx.x;
-    const bool lidar_out = lidar != nullptr, camera_out = cameras != nullptr || raw != nullptr;
+    constexpr int kPerScene = kLidar ? kLidarUnits : kCameraUnits;
     int used = 0;
     for (unsigned long long unit = blockIdx.x; unit < units; unit += gridDim.x) {
-        const unsigned long long scene_index = unit / kUnitsPerScene;
-        const int part = static_cast<int>(unit - scene_index * kUnitsPerScene);
+        const unsigned long long scene_index = unit / kPerScene;
+        const int part = static_cast<int>(unit - scene_index * kPerScene) + (kLidar ? 0 : kLidarUnits);
         const tb_sensor_scene *scene = scenes + scene_index;
-        const int sensors = scene->sensors; /* the same word for every thread: a CTA-uniform skip */
-        if (!(part < 2 ? (lidar_out && (sensors & TB_SENSOR_LIDAR)) : (camera_out && (sensors & TB_SENSOR_CAMERA))))
-            continue;
+        /* the same word for every thread: a CTA-uniform skip */
+        if (!(scene->sensors & (kLidar ? TB_SENSOR_LIDAR : TB_SENSOR_CAMERA))) continue;
         UnitScene &s = slots[used & 1];
         ++used;
         prepare_unit(s, scene, part);
-        const double qw = s.h.q[0], qx = s.h.q[1], qy = s.h.q[2], qz = s.h.q[3];
-
-        if (part < 2) {
-            /* LiDAR head `part` (sensors.c:31-49). */
-            float *out = lidar + scene_index * lidar_stride;
-            const double max_range = s.h.max_range;
-            /* SplitMix64 state before the draw of bin b is seed + (b + 1) * golden */
-            unsigned long long state = s.h.seed + static_cast<unsigned long long>(part * kUnitRays + t + 1) * kGolden;
-            int valid = 0;
-#pragma unroll 1
-            for (int k = 0; k < kUnitRays / kThreads; ++k, state += static_cast<unsigned long long>(kThreads) * kGolden) {
-                const int bin = part * kUnitRays + k * kThreads + t;
-                const unsigned long long hash = splitmix(state);
-                const bool blocked = (g_lidar_blocked[bin >> 5] >> (bin & 31)) & 1u;
-                float value = -1.0f;
-                if (!(static_cast<double>(hash & 0xffff) / 65536.0 < 0.005 || blocked)) {
-                    const Vec rw = rotate(qw, qx, qy, qz, Vec{g_lidar_x[bin], g_lidar_y[bin], g_lidar_z[bin]});
-                    int kind;
-                    bool exact;
-                    double range = trace<false>(s, rw, kind, exact);
-                    const double noise = (static_cast<double>((hash >> 16) & 0xffff) / 32768.0 - 1.0) * 0.02;
-                    range = fmax(0.05, fmin(max_range, range + noise));
-                    value = static_cast<float>(range);
-                    ++valid;
-                }
-                out[bin] = value;
-            }
-            if (lidar_valid) {
-                /* the last warp to finish writes the head's valid fraction */
-                valid = __reduce_add_sync(0xffffffffu, valid);
-                if ((t & 31) == 0) {
-                    atomicAdd(&s.valid_count, valid);
-                    __threadfence_block();
-                    if (atomicAdd(&s.warps_done, 1) == kWarps - 1)
-                        lidar_valid[scene_index * valid_stride + part] =
-                            static_cast<float>(atomicAdd(&s.valid_count, 0)) / 2048;
-                }
-            }
-        } else {
-            /* Half of camera view (part-2)/2 (sensors.c:71-79): 32 rows of 64. */
-            const int view = (part - 2) >> 1, half = (part - 2) & 1;
-#pragma unroll 1
-            for (int k = 0; k < kUnitRays / (4 * kThreads); ++k) {
-                const int local = half * kUnitRays + k * 4 * kThreads + 4 * t; /* pixel in the view */
-                const int pixel = view * 4096 + local;
-                uint32_t word = 0;
-#pragma unroll 1
-                for (int j = 0; j < 4; ++j) {
-                    const Vec dir = rotate(qw, qx, qy, qz,
-                                           Vec{g_camera_x[pixel + j], g_camera_y[pixel + j], g_camera_z[pixel + j]});
-                    int kind;
-                    bool exact;
-                    const double d = trace<true>(s, dir, kind, exact);
-                    word |= shade(s, d, kind, dir, exact) << (8 * j);
-                }
-                if (cameras)
-                    *reinterpret_cast<uint32_t *>(cameras + scene_index * kCameraPixels + pixel) = word;
-                if (raw) {
-                    /* each pixel as a 3 x 3 block of the 192 x 192 view (sensors.c:78) */
-                    const uint32_t p0 = word & 255u, p1 = (word >> 8) & 255u, p2 = (word >> 16) & 255u,
-                                   p3 = word >> 24;
-                    const uint32_t w0 = p0 | p0 << 8 | p0 << 16 | p1 << 24;
-                    const uint32_t w1 = p1 | p1 << 8 | p2 << 16 | p2 << 24;
-                    const uint32_t w2 = p2 | p3 << 8 | p3 << 16 | p3 << 24;
-                    const int y = local >> 6, x = local & 63;
-                    unsigned char *base = raw + scene_index * static_cast<unsigned long long>(TB_SENSOR_CAMERA_RAW_PIXELS) +
-                                          view * 36864 + 3 * x;
-#pragma unroll
-                    for (int dy = 0; dy < 3; ++dy) {
-                        uint32_t *row = reinterpret_cast<uint32_t *>(base + (3 * y + dy) * 192);
-                        row[0] = w0;
-                        row[1] = w1;
-                        row[2] = w2;
-                    }
-                }
-            }
-        }
+        if constexpr (kLidar)
+            render_lidar(s, part, scene_index, lidar, lidar_stride, lidar_valid, valid_stride);
+        else
+            render_camera(s, part, scene_index, cameras, raw);
     }
 }
 
@@ -601,6 +568,7 @@ constexpr int kMaxDevices = 64;
 bool g_tables_ready[kMaxDevices];
 int g_grid_cap[kMaxDevices];
 std::mutex g_tables_mutex;
+
 
 /* Cone of unit `part` over body-frame rays dirs[first .. first+count) (rays
  * with skip[i] set are never traced): unit axis, then cos and sin of the
@@ -673,7 +641,7 @@ bool ensure_tables(int dev) {
         cudaMemcpyToSymbol(g_camera_z, cz, sizeof cz) != cudaSuccess ||
         cudaMemcpyToSymbol(g_cone, cones, sizeof cones) != cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, sensors_kernel, kThreads, 0) != cudaSuccess)
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, sensors_kernel<false>, kThreads, 0) != cudaSuccess)
         return false;
     /* enough CTAs for many waves; each strides over the units */
     g_grid_cap[dev] = sms * (blocks > 0 ? blocks : 1) * 64;
@@ -699,10 +667,17 @@ extern "C" int tb_cuda_render_sensors_device(const tb_sensor_scene *device_scene
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
     if (!ensure_tables(dev)) return 0;
     cudaGetLastError(); /* report this launch only */
-    const unsigned long long units = static_cast<unsigned long long>(count) * kUnitsPerScene;
-    const unsigned long long grid = units < static_cast<unsigned long long>(g_grid_cap[dev]) ? units : g_grid_cap[dev];
-    sensors_kernel<<<static_cast<unsigned int>(grid), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        device_scenes, units, device_lidar, lidar_stride, device_lidar_valid, valid_stride, device_cameras,
-        device_raw_cameras);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned long long cap = static_cast<unsigned long long>(g_grid_cap[dev]);
+    if (device_lidar) {
+        const unsigned long long units = static_cast<unsigned long long>(count) * kLidarUnits;
+        sensors_kernel<true><<<static_cast<unsigned int>(units < cap ? units : cap), kThreads, 0, s>>>(
+            device_scenes, units, device_lidar, lidar_stride, device_lidar_valid, valid_stride, nullptr, nullptr);
+    }
+    if (device_cameras || device_raw_cameras) {
+        const unsigned long long units = static_cast<unsigned long long>(count) * kCameraUnits;
+        sensors_kernel<false><<<static_cast<unsigned int>(units < cap ? units : cap), kThreads, 0, s>>>(
+            device_scenes, units, nullptr, 0, nullptr, 0, device_cameras, device_raw_cameras);
+    }
     return cudaGetLastError() == cudaSuccess;
 }
