@@ -9,8 +9,9 @@ full: every rank compares its whole shard with the CPU oracle.
 
 BASELINE config 3 is seed 3 and 524,288 aircraft split into contiguous
 slices of B/N.  Each rank generates only its own slice, extracts it on its
-GPU through tb_cuda_extract_features_device, and the slices are gathered to
-rank 0 (shard.gather_features).  Rank 0 checks the strided subsample -- every
+GPU through tb_cuda_extract_features_device, and copies its device slice into
+one page-locked host buffer shared by all ranks (shard.SharedHostGather, the
+library's gather: no GPU collective).  Rank 0 checks the strided subsample -- every
 97th aircraft plus the first and last aircraft of every shard -- against the
 CPU oracle on inputs regenerated for just those indices (the generator is
 keyed by (seed, aircraft index), so any index can be rebuilt alone).  Every
@@ -33,7 +34,7 @@ import torch.distributed as dist  # noqa: E402
 import oracle  # noqa: E402
 import turbinator_c_b200 as tb  # noqa: E402
 from tests.parity import check_features  # noqa: E402
-from turbinator_c_b200.shard import gather_features, shard_range  # noqa: E402
+from turbinator_c_b200.shard import SharedHostGather, shard_range  # noqa: E402
 
 SEEDS = {"config3": 3, "config4": 4}
 
@@ -62,7 +63,14 @@ def main() -> int:
             except AssertionError as e:
                 print(f"config 4 mismatch on rank {rank}: {e}")
                 ok = False
-        full = gather_features(mine, total)
+        gatherer = SharedHostGather(total, 142)
+        gatherer.gather(out)
+        torch.cuda.synchronize()
+        dist.barrier()
+        full = gatherer.array
+        if not np.array_equal(full[first:first + count].view(np.uint32), mine.view(np.uint32)):
+            print(f"gather mismatch on rank {rank}")
+            ok = False
         if rank == 0 and not stress:
             idx = set(range(0, total, 97))
             for r in range(world):
@@ -79,6 +87,8 @@ def main() -> int:
             except AssertionError as e:
                 print(f"config 3 mismatch: {e}")
                 ok = False
+        full = None
+        gatherer.close()
         flag = torch.tensor([1 if ok else 0], device="cuda")
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         ok = bool(flag.item())
