@@ -1009,6 +1009,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     c3_max = statistics.median(max_over_ranks_list(c3_times))
     gather_bytes = total * tb.FEATURE_DIM * 4
     gather = {"ms": g_max * 1e3, "bytes_to_host": gather_bytes, "gbs": gather_bytes / g_max / 1e9,
+              "buffer": os.path.dirname(gatherer.path), "page_locked_ranks": sum(all_ranks(int(gatherer.registered))),
               "op": "each rank copies its [n,142] slice device-to-host into its offset of one page-locked "
                     "host buffer shared by all ranks (/dev/shm, cudaHostRegister per rank), concurrently; "
                     "no GPU collective",

@@ -119,9 +119,25 @@ def max_over_ranks(value: float, group=None) -> float:
     return float(t.item())
 
 
+def _shared_dir(nbytes: int) -> str:
+    """/dev/shm when it has room for the buffer (with 10 % to spare), else the
+    temporary directory: a mapped file anywhere is shared by the processes
+    that map it, and writing past a full tmpfs would kill them (SIGBUS)."""
+    import tempfile
+
+    try:
+        st = os.statvfs("/dev/shm")
+        if st.f_bavail * st.f_frsize >= 1.1 * nbytes:
+            return "/dev/shm"
+    except OSError:
+        pass
+    return tempfile.gettempdir()
+
+
 class SharedHostGather:
     """One host buffer of [total, width] float32 rows shared by all ranks of
-    a node (a /dev/shm file that every rank maps), with each rank's own rows
+    a node (a /dev/shm file, or a temporary-directory file when /dev/shm is
+    too small, that every rank maps), with each rank's own rows
     page-locked in its process so that a device-to-host copy lands there
     directly.  gather(slice) copies this rank's [count, width] device rows to
     its offset, asynchronously on `stream`; after a barrier every rank (rank 0
@@ -139,10 +155,11 @@ class SharedHostGather:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.total, self.width = total, width
         self.nbytes = total * width * 4
-        name = [f"{prefix}_{os.getpid()}_{uuid.uuid4().hex[:12]}" if self.rank == 0 else None]
+        name = [os.path.join(_shared_dir(self.nbytes), f"{prefix}_{os.getpid()}_{uuid.uuid4().hex[:12]}")
+                if self.rank == 0 else None]
         if self.world > 1:
             dist.broadcast_object_list(name, src=0, group=group)
-        self.path = os.path.join("/dev/shm", name[0])
+        self.path = name[0]
         if self.rank == 0:
             fd = os.open(self.path, os.O_CREAT | os.O_EXCL | os.O_RDWR, 0o600)
             os.ftruncate(fd, max(self.nbytes, PAGE))
@@ -163,10 +180,9 @@ class SharedHostGather:
         self._reg = (self._base + lo, hi - lo)
         self.registered = False
         if pin and hi > lo:
-            err = torch.cuda.cudart().cudaHostRegister(self._reg[0], self._reg[1], 0)
-            if int(err) != 0:
-                raise RuntimeError(f"cudaHostRegister of the shared gather buffer failed ({err})")
-            self.registered = True
+            # a refusal (e.g. file pages that the kernel will not pin) leaves the
+            # rows pageable: the copy still lands, through the driver's staging
+            self.registered = int(torch.cuda.cudart().cudaHostRegister(self._reg[0], self._reg[1], 0)) == 0
         self.mine = torch.from_numpy(self.array[self.first:self.first + self.count])
 
     def gather(self, device_rows, stream=None) -> None:
