@@ -38,6 +38,12 @@ BYTES_PER_SAMPLE_ACTOR_INPUTS = (OBS_DIM * 4 + MISSION_DIM * 4 + CAMERA_BYTES +
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libturbinator_cuda.so")
+#: The same library with the feature kernels' bounds checks compiled in
+#: (TB_FEATURES_DEBUG): tests load it in a separate process by setting
+#: TB_CUDA_LIBRARY to this path.
+DEBUG_LIB_PATH = os.path.join(_HERE, "libturbinator_cuda_debug.so")
+if os.environ.get("TB_CUDA_LIBRARY"):
+    LIB_PATH = os.environ["TB_CUDA_LIBRARY"]
 SYNTH_PATH = os.path.join(_HERE, "libtb_synth.so")
 
 _lib: Optional[ctypes.CDLL] = None

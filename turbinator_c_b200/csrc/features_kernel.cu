@@ -100,6 +100,25 @@ constexpr unsigned long long kDefaultWaitNs = 1000000000ull; /* ~1 s per wait */
 
 using namespace tb_pipe; /* staging primitives, tb_pipeline.cuh */
 
+/* Bounds checks of the debug build (compiled with TB_FEATURES_DEBUG): every
+ * global load and store index of the feature kernels is compared with the
+ * extent of its buffer (batch rows); an index outside ORs
+ * TB_FEATURE_STATUS_BOUNDS into the launching stream's status word, which
+ * tb_cuda_synchronize then reports, and the access is skipped.  In the
+ * product build the check is the constant true and compiles away. */
+__device__ __forceinline__ bool within(unsigned long long index, unsigned long long count, unsigned int *status) {
+#ifdef TB_FEATURES_DEBUG
+    if (index < count) return true;
+    atomicOr(status, TB_FEATURE_STATUS_BOUNDS);
+    return false;
+#else
+    (void)index;
+    (void)count;
+    (void)status;
+    return true;
+#endif
+}
+
 /* ------------------------------------------------------------------ */
 /* Per-feature arithmetic shared by both kernels. */
 
@@ -297,6 +316,12 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
                 break;
             }
             if (static_cast<long long>(sample) == a.stall_sample) continue; /* test hook */
+            /* debug build: a source row outside its buffer is not copied (the
+             * stage's consumers then time out and report it too) */
+            if (!within((sample + 1) * kObsDim - 1, a.batch * kObsDim, a.status) ||
+                !within((sample + 1) * kMissionDim - 1, a.batch * kMissionDim, a.status) ||
+                (cameras && !within((sample + 1) * R::camera_bytes - 1, a.batch * R::camera_bytes, a.status)))
+                continue;
             const uint32_t stage = smem_addr(stages + static_cast<size_t>(s) * R::stage_bytes);
             if (lane < kMissionDim) {
                 async_load4(stage + R::mission_off + 4 * lane, a.mission + sample * kMissionDim + lane);
@@ -387,15 +412,20 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
         lidar_band(r0, r1, r2, r3, sum, counts);
 
         float *f = a.features + sample * kFeatureDim;
-        if ((lane & 3) == 0)
-            f[62 + head * 32 + el_sector * 8 + (lane >> 2)] = lidar_sector_mean(sum, counts);
+        const unsigned long long out_first = sample * kFeatureDim, out_count = a.batch * kFeatureDim;
+        const int lidar_j = 62 + head * 32 + el_sector * 8 + (lane >> 2);
+        if ((lane & 3) == 0 && within(out_first + lidar_j, out_count, a.status))
+            f[lidar_j] = lidar_sector_mean(sum, counts);
         if constexpr (!kF32Cam) {
-            if (lane == 0 || lane == 2) f[126 + cam * 4 + qy * 2 + (lane >> 1)] = camera_feature(bytes);
+            const int cam_j = 126 + cam * 4 + qy * 2 + (lane >> 1);
+            if ((lane == 0 || lane == 2) && within(out_first + cam_j, out_count, a.status))
+                f[cam_j] = camera_feature(bytes);
         } else {
-            if (lane == 0 || lane == 8)
-                f[126 + cam * 4 + qy * 2 + (lane >> 3)] = __fdiv_rn(luma, 1024.0f * 255.0f);
+            const int cam_j = 126 + cam * 4 + qy * 2 + (lane >> 3);
+            if ((lane == 0 || lane == 8) && within(out_first + cam_j, out_count, a.status))
+                f[cam_j] = __fdiv_rn(luma, 1024.0f * 255.0f);
         }
-        if (t < 62) f[t] = scalar;
+        if (t < 62 && within(out_first + t, out_count, a.status)) f[t] = scalar;
     }
 }
 
@@ -409,11 +439,13 @@ __global__ void __launch_bounds__(kThreads, Ring<kF32Cam>::min_blocks)
  * slowest SMs: 7.1 TB/s of algorithmic bytes at 65,536 aircraft (the best
  * read stream measured on this pool) and the whole of a small batch (config
  * 1) requested in the first wave.  Same arithmetic as the staged kernel; no
- * waits, so no status word. */
+ * waits (the status word receives only the debug build's bounds bit). */
 __global__ void __launch_bounds__(kConsumerWarps * 32) features_flat_kernel(const float *__restrict__ obs,
                                                                            const float *__restrict__ mission,
                                                                            const unsigned char *__restrict__ cameras,
-                                                                           float *__restrict__ features) {
+                                                                           float *__restrict__ features,
+                                                                           unsigned long long batch,
+                                                                           unsigned int *__restrict__ status) {
     const unsigned long long sample = blockIdx.x;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -422,12 +454,19 @@ __global__ void __launch_bounds__(kConsumerWarps * 32) features_flat_kernel(cons
     const float *o = obs + sample * kObsDim;
     const float *m = mission + sample * kMissionDim;
 
-    const float4 *rows = reinterpret_cast<const float4 *>(o + kLidarOffset) + (head * 16 + el_sector * 4) * 32 + lane;
-    const float4 r0 = __ldcs(rows), r1 = __ldcs(rows + 32), r2 = __ldcs(rows + 64), r3 = __ldcs(rows + 96);
+    const int chunk = (head * 16 + el_sector * 4) * 32 + lane; /* float4 of the scan: 32 per row */
+    const float4 *rows = reinterpret_cast<const float4 *>(o + kLidarOffset) + chunk;
+    float4 r0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), r1 = r0, r2 = r0, r3 = r0;
+    if (within(sample * kObsDim + kLidarOffset + 4 * (chunk + 96) + 3, batch * kObsDim, status)) {
+        r0 = __ldcs(rows);
+        r1 = __ldcs(rows + 32);
+        r2 = __ldcs(rows + 64);
+        r3 = __ldcs(rows + 96);
+    }
     uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0, c2 = c0, c3 = c0;
-    if (cameras) {
-        const uint4 *half = reinterpret_cast<const uint4 *>(cameras + sample * kCameraBytes) + cam * 256 +
-                            qy * 128 + lane;
+    const int cam_chunk = cam * 256 + qy * 128 + lane; /* uint4 of the camera block */
+    if (cameras && within(sample * kCameraBytes + 16 * (cam_chunk + 96) + 15, batch * kCameraBytes, status)) {
+        const uint4 *half = reinterpret_cast<const uint4 *>(cameras + sample * kCameraBytes) + cam_chunk;
         c0 = __ldcs(half);
         c1 = __ldcs(half + 32);
         c2 = __ldcs(half + 64);
@@ -435,7 +474,9 @@ __global__ void __launch_bounds__(kConsumerWarps * 32) features_flat_kernel(cons
     }
     const int t = warp * 32 + lane;
     float scalar = 0.0f;
-    if (t < 62) scalar = scalar_feature(t, o, m);
+    if (t < 62 && within((sample + 1) * kObsDim - 1, batch * kObsDim, status) &&
+        within((sample + 1) * kMissionDim - 1, batch * kMissionDim, status))
+        scalar = scalar_feature(t, o, m);
 
     const uint32_t bytes = quadrant_bytes(c0, c1, c2, c3);
     float sum;
@@ -443,9 +484,14 @@ __global__ void __launch_bounds__(kConsumerWarps * 32) features_flat_kernel(cons
     lidar_band(r0, r1, r2, r3, sum, counts);
 
     float *f = features + sample * kFeatureDim;
-    if ((lane & 3) == 0) f[62 + head * 32 + el_sector * 8 + (lane >> 2)] = lidar_sector_mean(sum, counts);
-    if (lane == 0 || lane == 2) f[126 + cam * 4 + qy * 2 + (lane >> 1)] = camera_feature(bytes);
-    if (t < 62) f[t] = scalar;
+    const unsigned long long out_count = batch * kFeatureDim;
+    const int lidar_j = 62 + head * 32 + el_sector * 8 + (lane >> 2);
+    const int cam_j = 126 + cam * 4 + qy * 2 + (lane >> 1);
+    if ((lane & 3) == 0 && within(sample * kFeatureDim + lidar_j, out_count, status))
+        f[lidar_j] = lidar_sector_mean(sum, counts);
+    if ((lane == 0 || lane == 2) && within(sample * kFeatureDim + cam_j, out_count, status))
+        f[cam_j] = camera_feature(bytes);
+    if (t < 62 && within(sample * kFeatureDim + t, out_count, status)) f[t] = scalar;
 }
 
 /* ------------------------------------------------------------------ */
@@ -455,7 +501,7 @@ __global__ void __launch_bounds__(kConsumerWarps * 32) features_flat_kernel(cons
 template <bool kF32Cam>
 __global__ void __launch_bounds__(256) features_direct_kernel(const float *obs, const float *mission,
                                                               const void *cameras, float *features,
-                                                              unsigned long long batch) {
+                                                              unsigned long long batch, unsigned int *status) {
     const int lane = threadIdx.x & 31;
     const unsigned long long warps = (static_cast<unsigned long long>(gridDim.x) * blockDim.x) >> 5;
     for (unsigned long long sample = (static_cast<unsigned long long>(blockIdx.x) * blockDim.x +
@@ -464,6 +510,12 @@ __global__ void __launch_bounds__(256) features_direct_kernel(const float *obs, 
         const float *o = obs + sample * kObsDim;
         const float *m = mission + sample * kMissionDim;
         float *f = features + sample * kFeatureDim;
+        /* debug build: the rows this warp reads and writes lie in their buffers */
+        if (!within((sample + 1) * kObsDim - 1, batch * kObsDim, status) ||
+            !within((sample + 1) * kMissionDim - 1, batch * kMissionDim, status) ||
+            !within((sample + 1) * kFeatureDim - 1, batch * kFeatureDim, status) ||
+            (cameras && !within((sample + 1) * kCameraBytes - 1, batch * kCameraBytes, status)))
+            continue;
         for (int band = 0; band < 8; ++band) { /* head * 4 + el_sector */
             float sum = 0.0f;
             int counts = 0;
@@ -596,8 +648,13 @@ static int launch_features(const float *obs, const float *mission, const void *c
      * the staged kernel serves FP32 cameras and the test hooks */
     const bool flat = !kF32Cam && aligned_rows && !limited_grid && flat_choice >= 0;
     if (flat) {
+        unsigned int *status = tb_status_slot(stream);
+        if (!status) {
+            if (launch_error) *launch_error = static_cast<int>(cudaErrorInvalidDevice);
+            return 0;
+        }
         features_flat_kernel<<<static_cast<unsigned int>(batch), kConsumerWarps * 32, 0, s>>>(
-            obs, mission, static_cast<const unsigned char *>(cameras), features);
+            obs, mission, static_cast<const unsigned char *>(cameras), features, batch, status);
     } else if (aligned_rows) {
         unsigned int *status = tb_status_slot(stream);
         if (!status) {
@@ -635,8 +692,13 @@ static int launch_features(const float *obs, const float *mission, const void *c
         unsigned long long grid = (batch + 7) / 8; /* 8 warps of 32, one aircraft per warp */
         const unsigned long long cap = static_cast<unsigned long long>(info->sms) * 8;
         if (grid > cap) grid = cap;
+        unsigned int *status = tb_status_slot(stream);
+        if (!status) {
+            if (launch_error) *launch_error = static_cast<int>(cudaErrorInvalidDevice);
+            return 0;
+        }
         features_direct_kernel<kF32Cam>
-            <<<static_cast<unsigned int>(grid), 256, 0, s>>>(obs, mission, cameras, features, batch);
+            <<<static_cast<unsigned int>(grid), 256, 0, s>>>(obs, mission, cameras, features, batch, status);
     }
     st = cudaGetLastError();
     if (launch_error) *launch_error = static_cast<int>(st);

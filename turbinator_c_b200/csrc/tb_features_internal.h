@@ -18,8 +18,10 @@ enum {
     TB_FEATURE_DIM = 142
 };
 
-/* Status bits recorded by the kernels in their stream's status word. */
-enum { TB_FEATURE_STATUS_WAIT_TIMEOUT = 1u };
+/* Status bits recorded by the kernels in their stream's status word:
+ * a bounded pipeline wait expired; an index outside its buffer was caught
+ * (only the debug build, TB_FEATURES_DEBUG, checks indices). */
+enum { TB_FEATURE_STATUS_WAIT_TIMEOUT = 1u, TB_FEATURE_STATUS_BOUNDS = 2u };
 
 typedef struct tb_features_launch_opts {
     int force_direct;                 /* 1: use the plain-load kernel even for aligned rows */
