@@ -19,6 +19,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_PATH = os.path.join(HERE, "liboracle.so")
 # the renderer restatement with the product kernel's square-root skip (test build)
 ORACLE_SKIP_PATH = os.path.join(HERE, "liboracle_skip.so")
+ORACLE_FLOAT_PATH = os.path.join(HERE, "liboracle_float.so")
 REF_TRAINING_PATH = os.path.join(HERE, "_ref", "libtb_ref_training.so")
 REF_ONBOARD_PATH = os.path.join(HERE, "_ref", "libtb_ref_onboard.so")
 REF_ONBOARD_CR_PATH = os.path.join(HERE, "_ref", "libtb_ref_onboard_cr.so")
@@ -315,15 +316,39 @@ def _sensor_port_skip() -> ctypes.CDLL:
     return _oracle_skip
 
 
-def render_sensors_port(scenes, raw: bool = False, sqrt_skip: bool = False):
+_oracle_float = None
+
+
+def _sensor_port_float() -> ctypes.CDLL:
+    global _oracle_float
+    if _oracle_float is None:
+        if not os.path.exists(ORACLE_FLOAT_PATH):
+            raise RuntimeError(f"{ORACLE_FLOAT_PATH} missing: run `make -C oracle`")
+        l = ctypes.CDLL(ORACLE_FLOAT_PATH)
+        l.oracle_render_sensors.restype = None
+        l.oracle_render_sensors.argtypes = [_vp, ctypes.c_int64, _vp, ctypes.c_int64, _vp, ctypes.c_int64, _vp, _vp]
+        l.oracle_float_pixels.restype = ctypes.c_uint64
+        l.oracle_float_pixels.argtypes = []
+        _oracle_float = l
+    return _oracle_float
+
+
+def float_pixels() -> int:
+    """Camera pixels the float-decision build has decided so far in this process."""
+    return int(_sensor_port_float().oracle_float_pixels())
+
+
+def render_sensors_port(scenes, raw: bool = False, sqrt_skip: bool = False, float_camera: bool = False):
     """Restated renderers (sensors_oracle.c): (lidar [n,4096], valid [n,2],
     cameras [n,16384], raw [n,147456] or None); unrendered rows keep NaN / 0.
     sqrt_skip=True renders with the test build that drops spheres without the
-    square root under the product kernel's condition."""
+    square root under the product kernel's condition; float_camera=True with
+    the test build that first offers every camera pixel to the product
+    kernel's float decision (tb_camera_float.h)."""
     scenes = np.ascontiguousarray(scenes)
     n = scenes.shape[0]
     lidar, valid, cams, raws = _sensor_outputs(n, raw)
-    port = _sensor_port_skip() if sqrt_skip else _sensor_port()
+    port = _sensor_port_skip() if sqrt_skip else (_sensor_port_float() if float_camera else _sensor_port())
     port.oracle_render_sensors(_addr(scenes), n, _addr(lidar), 4096, _addr(valid), 2, _addr(cams), _addr(raws))
     return lidar, valid, cams, raws
 

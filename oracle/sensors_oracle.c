@@ -207,13 +207,87 @@ static uint8_t oshade(double d, int kind, ovec dir) {
     return (uint8_t)oclamp(round(luma * 255), 0, 255);
 }
 
+#ifdef ORACLE_FLOAT_CAMERA
+/* Built with ORACLE_FLOAT_CAMERA (only into oracle/liboracle_float.so, a test
+ * build): each camera pixel is first offered to the product kernel's float
+ * decision (turbinator_c_b200/csrc/tb_camera_float.h), with the same per-view
+ * eligibility (a rotation, no shelf, no reachable dome, bounded geometry)
+ * and every sphere of the scene in its list; only pixels it declines are
+ * traced in double.  The test renders must equal the unmodified
+ * restatement's bit for bit.  oracle_float_pixels() counts the pixels the
+ * float decision took. */
+#include "../turbinator_c_b200/csrc/tb_camera_float.h"
+static uint64_t g_float_pixels;
+uint64_t oracle_float_pixels(void) { return g_float_pixels; }
+
+static int ofloat_view(const tb_sensor_scene *s, ovec o, tbf_unit *u, tbf_sphere *sp, float *margin, int *n) {
+    const double *q = s->attitude;
+    const int bwb = obwb(s->scenario), arena = oarena(s->scenario);
+    const double best0 = bwb ? fmax(s->lidar_max, 120) : s->lidar_max;
+    const double norm2 = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
+    if (!(fabs(norm2 - 1.0) < 1e-9) || s->scenario == 10) return 0;
+    if (!(fabs(o.x) < 1e6 && fabs(o.y) < 1e6 && fabs(o.z) < 1e6 && best0 < 1e6)) return 0;
+    if (arena) {
+        const double dome = bwb ? 300.0 : s->dome_radius;
+        const double rho = sqrt(o.x * o.x + o.y * o.y);
+        if (!(dome - rho > best0 * (1 + 1e-9) + 1e-9)) return 0;
+    }
+    u->qw = (float)q[0]; u->qx = (float)q[1]; u->qy = (float)q[2]; u->qz = (float)q[3];
+    u->oz = (float)o.z;
+    u->sky_fog = (float)(0.75 + 0.25 * exp(-best0 / 80));
+    u->best0 = best0;
+    int k = 0;
+    const int obstacles = oclamp_count(s->obstacle_count, TB_SENSOR_MAX_OBSTACLES);
+    const int balls = oclamp_count(s->ball_count, TB_SENSOR_MAX_BALLS);
+    double c[TB_SENSOR_MAX_OBSTACLES + 1 + TB_SENSOR_MAX_BALLS][4];
+    for (int i = 0; i < obstacles; i++, k++) {
+        c[k][0] = s->obstacles[i][0]; c[k][1] = s->obstacles[i][1]; c[k][2] = s->obstacles[i][2];
+        c[k][3] = s->obstacles[i][3];
+    }
+    if (arena) {
+        c[k][0] = s->opponent[0]; c[k][1] = s->opponent[1]; c[k][2] = s->opponent[2]; c[k][3] = bwb ? 0.75 : 0.45;
+        k++;
+    }
+    for (int i = 0; i < balls; i++, k++) {
+        c[k][0] = s->balls[i][0]; c[k][1] = s->balls[i][1]; c[k][2] = s->balls[i][2]; c[k][3] = 0.25;
+    }
+    for (int i = 0; i < k; i++) {
+        const double ocx = o.x - c[i][0], ocy = o.y - c[i][1], ocz = o.z - c[i][2];
+        const double occ = ocx * ocx + ocy * ocy + ocz * ocz, rr = c[i][3] * c[i][3];
+        sp[i].x = (float)ocx; sp[i].y = (float)ocy; sp[i].z = (float)ocz; sp[i].w = (float)(rr - occ);
+        margin[i] = occ + rr < 1e30 ? (float)(TBF_SPHERE_MARGIN * (occ + rr)) : INFINITY;
+    }
+    *n = k;
+    return 1;
+}
+#endif
+
 void oracle_render_camera(const tb_sensor_scene *s, uint8_t *pixels, uint8_t *raw) {
     for (int view = 0; view < 4; view++) {
         ovec mount = view < 2 ? ov(0.42, 0.42, view == 0 ? 0.13 : 0.08) : ov(0, 0, view == 2 ? -0.5 : 0.5);
         ovec o = oorigin(s, mount);
+#ifdef ORACLE_FLOAT_CAMERA
+        tbf_unit fu;
+        tbf_sphere fsp[TB_SENSOR_MAX_OBSTACLES + 1 + TB_SENSOR_MAX_BALLS];
+        float fmargin[TB_SENSOR_MAX_OBSTACLES + 1 + TB_SENSOR_MAX_BALLS];
+        int fn = 0;
+        const int float_view = ofloat_view(s, o, &fu, fsp, fmargin, &fn);
+#endif
         for (int y = 0; y < 64; y++)
             for (int x = 0; x < 64; x++) {
-                ovec dir = oturn(s->attitude, oview_ray(view, (x + 0.5 - 32) / 32, (y + 0.5 - 32) / 32));
+                ovec body = oview_ray(view, (x + 0.5 - 32) / 32, (y + 0.5 - 32) / 32);
+#ifdef ORACLE_FLOAT_CAMERA
+                unsigned int fb;
+                if (float_view && tbf_camera_pixel(&fu, fsp, fmargin, fn, (float)body.x, (float)body.y, (float)body.z,
+                                                   &fb)) {
+                    ++g_float_pixels;
+                    if (pixels) pixels[view * 4096 + y * 64 + x] = (uint8_t)fb;
+                    if (raw)
+                        for (int dy = 0; dy < 3; dy++) memset(raw + view * 36864 + (3 * y + dy) * 192 + 3 * x, (int)fb, 3);
+                    continue;
+                }
+#endif
+                ovec dir = oturn(s->attitude, body);
                 int kind;
                 double d = ocast(s, o, dir, &kind);
                 uint8_t px = oshade(d, kind, dir);

@@ -124,3 +124,31 @@ def test_sqrt_skip_never_changes_a_render(kind):
                  oracle.render_sensors_port(scenes, raw=kind == "edge"), f"square-root skip/{kind}")
     if kind in ("max", "random"):
         assert oracle.sqrt_skips() > before, "the skip never fired"
+
+
+@pytest.mark.parametrize("kind", ["flight", "max", "random", "edge", "episodes"])
+def test_float_camera_decision_never_changes_a_byte(kind):
+    """The product kernel first offers each camera pixel to a float decision
+    (turbinator_c_b200/csrc/tb_camera_float.h) and traces it in double only
+    when that declines.  The same header, built into a copy of the restated
+    renderer (oracle/liboracle_float.so, plain IEEE float arithmetic as on the
+    GPU, glibc's expf in place of CUDA's __expf), must give every camera byte
+    of the double renderer; on flight scenes it must decide most pixels, or
+    the test proves little."""
+    if kind in ("flight", "max"):
+        scenes = synthetic_scenes(400 + len(kind), 256, balls=kind)
+    elif kind == "random":
+        scenes = np.concatenate([random_scenes(41, 128), random_scenes(42, 128, unit_attitude=False)])
+    elif kind == "edge":
+        scenes = edge_scenes()
+    else:
+        n = 112
+        idx = np.arange(n)
+        scenes, _, _, _ = oracle.simulate_sensor_scenes(idx % 28, idx + 3000, (idx * 37) % 800, idx % 2, SCENE_DTYPE)
+    before = oracle.float_pixels()
+    _assert_same(oracle.render_sensors_port(scenes, raw=kind == "edge", float_camera=True),
+                 oracle.render_sensors_port(scenes, raw=kind == "edge"), f"float camera/{kind}")
+    decided = oracle.float_pixels() - before
+    if kind == "flight":
+        assert decided > 0.5 * 16384 * len(scenes), decided
+    print(f"\n{kind}: {decided} of {16384 * len(scenes)} camera pixels decided in float")

@@ -56,6 +56,7 @@
 
 #include <mutex>
 
+#include "tb_camera_float.h"
 #include "tb_sensor_rays.h"
 #include "turbinator/sim/cuda_sensors.h"
 
@@ -88,6 +89,8 @@ static_assert(kThreads >= 32 * kSphereWarps && kUnitRays % (4 * kThreads) == 0, 
 __device__ double g_lidar_x[kLidarBins], g_lidar_y[kLidarBins], g_lidar_z[kLidarBins];
 __device__ unsigned int g_lidar_blocked[kLidarBins / 32];
 __device__ double g_camera_x[kCameraPixels], g_camera_y[kCameraPixels], g_camera_z[kCameraPixels];
+/* The same camera directions rounded to float, for the float pixel test. */
+__device__ float g_camera_fx[kCameraPixels], g_camera_fy[kCameraPixels], g_camera_fz[kCameraPixels];
 /* Per unit kind: body-frame cone axis (unit) and cos, sin of its half-angle
  * widened by 1e-6 rad. */
 __device__ double g_cone[kUnitsPerScene][5];
@@ -123,6 +126,7 @@ struct UnitHead {
     int dome;                        /* the dome can be hit before the sky distance */
     int cull;                        /* the attitude is a rotation: culling allowed */
     int shelf;                       /* scenario 10's raised ground at z = 9, x >= 20 */
+    int float_camera;                /* camera pixels may be decided in float (tb_camera_float.h) */
 };
 
 /* One unit's scene, prepared for tracing from one origin. */
@@ -132,6 +136,7 @@ struct UnitScene {
     double rr[kMaxSpheres];     /* radius^2 */
     float4 f_oc[kMaxSpheres];   /* float copies for the miss test: origin - centre, rr - |oc|^2 */
     float f_margin[kMaxSpheres]; /* the miss test's error margin (+inf: no float test) */
+    float f_margin_ray[kMaxSpheres]; /* the same with a float ray direction (tb_camera_float.h) */
     UnitHead h;
     int kept_obstacles, kept_opponent, kept_total; /* the unit's list, in trace order */
     unsigned int keep_mask[kSphereWarps], obst_mask[kSphereWarps], opp_mask[kSphereWarps];
@@ -357,6 +362,10 @@ __device__ __forceinline__ void unit_head(UnitHead &h, const tb_sensor_scene *__
     h.dome = !(h.cull && dome - rho > h.best0 * (1 + 1e-9) + 1e-9);
     h.shelf = scenario == 10;
     h.arena = arena;
+    /* float camera pixels: a rotation, no shelf, no reachable dome, finite
+     * geometry of modest size (tb_camera_float.h's bounds) */
+    h.float_camera = h.cull && !h.shelf && !(arena && h.dome) && fabs(ox) < 1e6 && fabs(oy) < 1e6 &&
+                     fabs(oz) < 1e6 && h.best0 < 1e6;
     h.n_obstacles = min(max(scene->obstacle_count, 0), TB_SENSOR_MAX_OBSTACLES);
     h.n_balls = min(max(scene->ball_count, 0), TB_SENSOR_MAX_BALLS);
     /* sensors.c:30: rng ^ step_index * golden ^ player * 257 */
@@ -432,6 +441,7 @@ __device__ __forceinline__ void prepare_unit(UnitScene &s, const tb_sensor_scene
             s.f_oc[pos] = make_float4(__double2float_rn(ocx), __double2float_rn(ocy), __double2float_rn(ocz),
                                       __double2float_rn(rr - occ));
             s.f_margin[pos] = float_test ? __double2float_rn(0x1.0p-18 * (occ + rr)) : INFINITY;
+            s.f_margin_ray[pos] = float_test ? __double2float_rn(TBF_SPHERE_MARGIN * (occ + rr)) : INFINITY;
         }
         if (t == 0) {
             int total = 0, kept_obst = 0, kept_opp = 0;
@@ -500,6 +510,16 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
                                               unsigned char *cameras, unsigned char *raw) {
     const int t = threadIdx.x;
     const double qw = s.h.q[0], qx = s.h.q[1], qy = s.h.q[2], qz = s.h.q[3];
+    const bool float_unit = s.h.float_camera;
+    tbf_unit fu;
+    fu.qw = __double2float_rn(qw);
+    fu.qx = __double2float_rn(qx);
+    fu.qy = __double2float_rn(qy);
+    fu.qz = __double2float_rn(qz);
+    fu.oz = __double2float_rn(s.h.origin[2]);
+    fu.sky_fog = __double2float_rn(s.h.sky_fog);
+    fu.best0 = s.h.best0;
+    const tbf_sphere *fspheres = reinterpret_cast<const tbf_sphere *>(s.f_oc);
     const int view = (part - 2) >> 1, half = (part - 2) & 1;
 #pragma unroll 1
     for (int k = 0; k < kUnitRays / (4 * kThreads); ++k) {
@@ -508,11 +528,16 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
         uint32_t word = 0;
 #pragma unroll 1
         for (int j = 0; j < 4; ++j) {
-            const Vec dir = rotate(qw, qx, qy, qz,
-                                   Vec{g_camera_x[pixel + j], g_camera_y[pixel + j], g_camera_z[pixel + j]});
-            int kind;
-            const double d = trace(s, dir, kind);
-            word |= shade(s, d, kind, dir.z) << (8 * j);
+            unsigned int byte;
+            if (!(float_unit && tbf_camera_pixel(&fu, fspheres, s.f_margin_ray, s.kept_total, g_camera_fx[pixel + j],
+                                                 g_camera_fy[pixel + j], g_camera_fz[pixel + j], &byte))) {
+                const Vec dir = rotate(qw, qx, qy, qz,
+                                       Vec{g_camera_x[pixel + j], g_camera_y[pixel + j], g_camera_z[pixel + j]});
+                int kind;
+                const double d = trace(s, dir, kind);
+                byte = shade(s, d, kind, dir.z);
+            }
+            word |= byte << (8 * j);
         }
         if (cameras)
             *reinterpret_cast<uint32_t *>(cameras + scene_index * kCameraPixels + pixel) = word;
@@ -610,6 +635,7 @@ bool ensure_tables(int dev) {
     static bool built = false;
     static double lx[kLidarBins], ly[kLidarBins], lz[kLidarBins];
     static double cx[kCameraPixels], cy[kCameraPixels], cz[kCameraPixels];
+    static float cfx[kCameraPixels], cfy[kCameraPixels], cfz[kCameraPixels];
     static unsigned int mask[kLidarBins / 32];
     static double cones[kUnitsPerScene][5];
     if (!built) {
@@ -625,6 +651,9 @@ bool ensure_tables(int dev) {
             cx[i] = camera_dirs[3 * i];
             cy[i] = camera_dirs[3 * i + 1];
             cz[i] = camera_dirs[3 * i + 2];
+            cfx[i] = static_cast<float>(cx[i]);
+            cfy[i] = static_cast<float>(cy[i]);
+            cfz[i] = static_cast<float>(cz[i]);
         }
         for (int h = 0; h < 2; ++h) unit_cone(lx, ly, lz, h * kUnitRays, kUnitRays, blocked, cones[h]);
         for (int p = 2; p < kUnitsPerScene; ++p)
@@ -639,6 +668,9 @@ bool ensure_tables(int dev) {
         cudaMemcpyToSymbol(g_camera_x, cx, sizeof cx) != cudaSuccess ||
         cudaMemcpyToSymbol(g_camera_y, cy, sizeof cy) != cudaSuccess ||
         cudaMemcpyToSymbol(g_camera_z, cz, sizeof cz) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_camera_fx, cfx, sizeof cfx) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_camera_fy, cfy, sizeof cfy) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_camera_fz, cfz, sizeof cfz) != cudaSuccess ||
         cudaMemcpyToSymbol(g_cone, cones, sizeof cones) != cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, sensors_kernel<false>, kThreads, 0) != cudaSuccess)
