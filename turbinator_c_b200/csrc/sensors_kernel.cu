@@ -521,24 +521,53 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
     fu.best0 = s.h.best0;
     const tbf_sphere *fspheres = reinterpret_cast<const tbf_sphere *>(s.f_oc);
     const int view = (part - 2) >> 1, half = (part - 2) & 1;
+    /* Each warp owns 256 pixels of the unit: rows of 128 at 128 w and
+     * 1024 + 128 w, lane l pixels 4l..4l+3 of each.  Pass 1 decides them in
+     * float; the undecided ones go to a per-warp queue, which pass 2 traces
+     * in double one pixel per lane (so a warp pays the double path only for
+     * its undecided pixels, not whenever one lane has one); pass 3 writes the
+     * bytes four to a 32-bit store. */
+    __shared__ __align__(16) unsigned char warp_bytes[kWarps][256];
+    __shared__ unsigned char warp_queue[kWarps][256];
+    const int warp = t >> 5, lane = t & 31;
+    unsigned char *bytes = warp_bytes[warp];
+    unsigned char *queue = warp_queue[warp];
+    const int first = view * 4096 + half * kUnitRays + warp * 128; /* pixel of the warp's entry 0 */
+    auto pixel_of = [first](int e) { return first + (e >> 7) * 1024 + (e & 127); };
+    int queued = 0;
 #pragma unroll 1
-    for (int k = 0; k < kUnitRays / (4 * kThreads); ++k) {
-        const int local = half * kUnitRays + k * 4 * kThreads + 4 * t; /* pixel in the view */
-        const int pixel = view * 4096 + local;
-        uint32_t word = 0;
+    for (int k = 0; k < 2; ++k) {
 #pragma unroll 1
         for (int j = 0; j < 4; ++j) {
-            unsigned int byte;
-            if (!(float_unit && tbf_camera_pixel(&fu, fspheres, s.f_margin_ray, s.kept_total, g_camera_fx[pixel + j],
-                                                 g_camera_fy[pixel + j], g_camera_fz[pixel + j], &byte))) {
-                const Vec dir = rotate(qw, qx, qy, qz,
-                                       Vec{g_camera_x[pixel + j], g_camera_y[pixel + j], g_camera_z[pixel + j]});
-                int kind;
-                const double d = trace(s, dir, kind);
-                byte = shade(s, d, kind, dir.z);
-            }
-            word |= byte << (8 * j);
+            const int e = k * 128 + 4 * lane + j;
+            const int pixel = pixel_of(e);
+            unsigned int byte = 0;
+            const bool done = float_unit && tbf_camera_pixel(&fu, fspheres, s.f_margin_ray, s.kept_total,
+                                                             g_camera_fx[pixel], g_camera_fy[pixel],
+                                                             g_camera_fz[pixel], &byte);
+            if (done) bytes[e] = static_cast<unsigned char>(byte);
+            const unsigned int pending = __ballot_sync(0xffffffffu, !done);
+            if (!done) queue[queued + __popc(pending & ((1u << lane) - 1u))] = static_cast<unsigned char>(e);
+            queued += __popc(pending);
         }
+    }
+    __syncwarp();
+#pragma unroll 1
+    for (int q = lane; q < queued; q += 32) {
+        const int e = queue[q];
+        const int pixel = pixel_of(e);
+        const Vec dir = rotate(qw, qx, qy, qz, Vec{g_camera_x[pixel], g_camera_y[pixel], g_camera_z[pixel]});
+        int kind;
+        const double d = trace(s, dir, kind);
+        bytes[e] = static_cast<unsigned char>(shade(s, d, kind, dir.z));
+    }
+    __syncwarp();
+#pragma unroll 1
+    for (int k = 0; k < 2; ++k) {
+        const int e = k * 128 + 4 * lane;
+        const int pixel = pixel_of(e);
+        const int local = pixel - view * 4096; /* pixel in the view */
+        const uint32_t word = *reinterpret_cast<const uint32_t *>(bytes + e);
         if (cameras)
             *reinterpret_cast<uint32_t *>(cameras + scene_index * kCameraPixels + pixel) = word;
         if (raw) {
@@ -560,6 +589,7 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
             }
         }
     }
+    __syncwarp(); /* the buffers are refilled by the next unit */
 }
 
 template <bool kLidar>
