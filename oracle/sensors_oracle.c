@@ -211,7 +211,7 @@ static uint8_t oshade(double d, int kind, ovec dir) {
 /* Built with ORACLE_FLOAT_CAMERA (only into oracle/liboracle_float.so, a test
  * build): each camera pixel is first offered to the product kernel's float
  * decision (turbinator_c_b200/csrc/tb_camera_float.h), with the same per-view
- * eligibility (a rotation, no shelf, bounded geometry) and dome flag
+ * eligibility (a rotation, no shelf, no reachable dome, bounded geometry)
  * and every sphere of the scene in its list; only pixels it declines are
  * traced in double.  The test renders must equal the unmodified
  * restatement's bit for bit.  oracle_float_pixels() counts the pixels the
@@ -227,17 +227,17 @@ static int ofloat_view(const tb_sensor_scene *s, ovec o, tbf_unit *u, tbf_sphere
     const double norm2 = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
     if (!(fabs(norm2 - 1.0) < 1e-9) || s->scenario == 10) return 0;
     if (!(fabs(o.x) < 1e6 && fabs(o.y) < 1e6 && fabs(o.z) < 1e6 && best0 < 1e6)) return 0;
-    const double dome = bwb ? 300.0 : s->dome_radius;
-    if (!(dome < 1e6)) return 0;
-    const double rho = sqrt(o.x * o.x + o.y * o.y);
-    u->dome = arena && !(dome - rho > best0 * (1 + 1e-9) + 1e-9);
-    u->ox = (float)o.x;
-    u->oy = (float)o.y;
-    u->dome_cc = (float)(o.x * o.x + o.y * o.y - dome * dome);
+    if (arena) {
+        const double dome = bwb ? 300.0 : s->dome_radius;
+        const double rho = sqrt(o.x * o.x + o.y * o.y);
+        if (!(dome - rho > best0 * (1 + 1e-9) + 1e-9)) return 0;
+    }
     u->qw = (float)q[0]; u->qx = (float)q[1]; u->qy = (float)q[2]; u->qz = (float)q[3];
     u->oz = (float)o.z;
     u->sky_fog = (float)(0.75 + 0.25 * exp(-best0 / 80));
     u->best0 = best0;
+    u->best0_lo = (float)(best0 * (1 - 1e-6));
+    u->best0_hi = (float)(best0 * (1 + 1e-6));
     int k = 0;
     const int obstacles = oclamp_count(s->obstacle_count, TB_SENSOR_MAX_OBSTACLES);
     const int balls = oclamp_count(s->ball_count, TB_SENSOR_MAX_BALLS);

@@ -362,10 +362,10 @@ __device__ __forceinline__ void unit_head(UnitHead &h, const tb_sensor_scene *__
     h.dome = !(h.cull && dome - rho > h.best0 * (1 + 1e-9) + 1e-9);
     h.shelf = scenario == 10;
     h.arena = arena;
-    /* float camera pixels: a rotation, no shelf, finite geometry of modest
-     * size (tb_camera_float.h's bounds) */
-    h.float_camera = h.cull && !h.shelf && fabs(ox) < 1e6 && fabs(oy) < 1e6 && fabs(oz) < 1e6 &&
-                     h.best0 < 1e6 && dome < 1e6;
+    /* float camera pixels: a rotation, no shelf, no reachable dome, finite
+     * geometry of modest size (tb_camera_float.h's bounds) */
+    h.float_camera = h.cull && !h.shelf && !(arena && h.dome) && fabs(ox) < 1e6 && fabs(oy) < 1e6 &&
+                     fabs(oz) < 1e6 && h.best0 < 1e6;
     h.n_obstacles = min(max(scene->obstacle_count, 0), TB_SENSOR_MAX_OBSTACLES);
     h.n_balls = min(max(scene->ball_count, 0), TB_SENSOR_MAX_BALLS);
     /* sensors.c:30: rng ^ step_index * golden ^ player * 257 */
@@ -519,10 +519,8 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
     fu.oz = __double2float_rn(s.h.origin[2]);
     fu.sky_fog = __double2float_rn(s.h.sky_fog);
     fu.best0 = s.h.best0;
-    fu.dome = s.h.arena && s.h.dome;
-    fu.ox = __double2float_rn(s.h.origin[0]);
-    fu.oy = __double2float_rn(s.h.origin[1]);
-    fu.dome_cc = __double2float_rn(s.h.dome_cc);
+    fu.best0_lo = __double2float_rn(s.h.best0 * (1 - 1e-6));
+    fu.best0_hi = __double2float_rn(s.h.best0 * (1 + 1e-6));
     const tbf_sphere *fspheres = reinterpret_cast<const tbf_sphere *>(s.f_oc);
     const int view = (part - 2) >> 1, half = (part - 2) & 1;
     /* Each warp owns 256 pixels of the unit: rows of 128 at 128 w and

@@ -9,8 +9,10 @@
  * tbf_camera_pixel returns 1 and the byte when it can prove it; 0 when the
  * caller must trace the ray in double.  It handles the rays whose double
  * trace ends at the sky or the ground with every sphere missed, in units
- * whose attitude is a rotation and that have no raised shelf (the caller
- * checks those per unit), or at the arena dome (tbf_dome).
+ * whose attitude is a rotation and that have no raised shelf and no arena
+ * dome within the sky distance (the caller checks those per unit).  (A float
+ * dome test was written, checked bit for bit and dropped: it decided more
+ * pixels but cost more time than it saved.)
  *
  * Error bounds, u = 2^-24, all arithmetic plain float (the kernel's file is
  * built without contraction):
@@ -24,8 +26,10 @@
  *    1.2e-4 (L^2 + r^2): a float value below minus it proves "no hit".
  *  - Ground: the simulator tests d.z < -1e-5, then t = (0 - oz) / d.z
  *    against 0.05 and the sky distance.  d.z is decided when it clears -1e-5
- *    by TBF_ED; t in float is within rel = TBF_ED / (|dz| - TBF_ED) + 4 u
- *    (relative) of the double t, and the tests use t (1 -+ 2 rel).
+ *    by TBF_ED; t in float (a division within 2 ulp) is within
+ *    rel = TBF_ED / (|dz| - TBF_ED) + 6 u (relative) of the double t, and
+ *    the tests use t (1 -+ 2 rel), in float with 4 u more for their own
+ *    rounding, against 0.05 and the sky distance widened by 1e-6 relative.
  *  - Byte: round(luma * fog * 255) with luma from d.z and fog from the sky
  *    factor or from t through expf (CUDA's __expf, within 3e-7 for arguments
  *    <= 0, checked exhaustively by a GPU test; glibc's expf is closer).  The
@@ -42,9 +46,11 @@
 #ifdef __CUDACC__
 #define TBF_FN static __device__ __forceinline__
 #define TBF_EXPF(x) __expf(x)
+#define TBF_FDIV(a, b) __fdividef((a), (b)) /* within 2 ulp for |b| in [2^-126, 2^126] */
 #else
 #define TBF_FN static inline
 #define TBF_EXPF(x) expf(x)
+#define TBF_FDIV(a, b) ((a) / (b))
 #endif
 
 #define TBF_ED 8e-6f                 /* per-component bound on the float direction's error */
@@ -58,44 +64,8 @@ typedef struct tbf_unit {
     float oz;
     float sky_fog;
     double best0;
-    int dome;          /* the arena dome can be hit before the sky distance */
-    float ox, oy;      /* origin x, y (dome test) */
-    float dome_cc;     /* ox^2 + oy^2 - dome^2, rounded from the double value */
+    float best0_lo, best0_hi; /* best0 (1 -+ 1e-6) in float: bounds for float comparisons */
 } tbf_unit;
-
-/* The dome's exit distance td = (-qb + sqrt(qb^2 - 4 qa qc)) / (2 qa) along
- * the float direction, with qa = dx^2 + dy^2, qb = 2 (ox dx + oy dy),
- * qc = dome_cc (trace's expressions), and a bound on |td - td_double|.
- * Returns 1 with *td, *err when the dome test is decided and hit-capable,
- * 0 when it certainly returns no hit (qa <= 1e-9 or disc < 0), -1 when it
- * cannot tell.  Bounds (R = |ox| + |oy|, E = TBF_ED): qa within
- * 2.9 E + 4u, qb within 2 R (E + 4u), qc within u |qc|; the discriminant and
- * td bounds follow from those by first-order propagation, doubled. */
-TBF_FN int tbf_dome(const tbf_unit *u, float dx, float dy, float *td, float *err) {
-    const float qa = dx * dx + dy * dy;
-    const float eqa = 2.9f * TBF_ED + 4.0f * TBF_U;
-    if (qa + eqa <= 1e-9f) return 0;
-    if (!(qa - eqa > 1e-9f) || !(qa > 4.0f * eqa)) return -1;
-    const float R = fabsf(u->ox) + fabsf(u->oy);
-    const float qb = 2.0f * (u->ox * dx + u->oy * dy);
-    const float eqb = 2.0f * R * (TBF_ED + 4.0f * TBF_U);
-    const float qc = u->dome_cc;
-    const float eqc = TBF_U * fabsf(qc);
-    const float disc = qb * qb - 4.0f * qa * qc;
-    const float B = fabsf(qb), C = fabsf(qc);
-    const float edisc = 2.0f * (2.0f * B * eqb + eqb * eqb + 4.0f * (qa * eqc + C * eqa + eqa * eqc) +
-                                3.0f * TBF_U * (B * B + 4.0f * qa * C));
-    if (disc + edisc < 0.0f) return 0;
-    if (!(disc > 4.0f * edisc)) return -1;
-    const float root = sqrtf(disc);
-    const float eroot = edisc / root + TBF_U * root;
-    const float num = -qb + root;
-    const float enum_ = eqb + eroot + TBF_U * (B + root);
-    if (!(fabsf(num) > 4.0f * enum_)) return -1;
-    *td = num / (2.0f * qa);
-    *err = 2.0f * fabsf(*td) * (enum_ / fabsf(num) + eqa / qa + 3.0f * TBF_U);
-    return 1;
-}
 
 /* Per sphere: origin - centre (x, y, z) and r^2 - |origin - centre|^2 (w). */
 typedef struct tbf_sphere {
@@ -115,43 +85,24 @@ TBF_FN int tbf_camera_pixel(const tbf_unit *u, const tbf_sphere *spheres, const 
     }
     int ground = 0;
     float t = 0.0f, rel = 0.0f;
-    double best_lo = u->best0, best_hi = u->best0; /* trace's `best` after the ground test */
     if (dz < -1e-5f - TBF_ED) {
-        t = -u->oz / dz;
-        rel = TBF_ED / (-dz - TBF_ED) + 4.0f * TBF_U;
+        /* the division is within 2 ulp (CUDA's __fdividef; exact on the CPU):
+         * t within rel of the double t, rel an over-estimate (1.001 covers the
+         * error of its own division) */
+        t = TBF_FDIV(-u->oz, dz);
+        rel = 1.001f * TBF_FDIV(TBF_ED, -dz - TBF_ED) + 6.0f * TBF_U;
         if (!(rel < 0.01f)) return 0;
-        const double lo = (double)t * (1.0 - 2.0 * rel), hi = (double)t * (1.0 + 2.0 * rel);
-        if (lo > 0.05 && hi < u->best0) {
+        /* t (1 -+ 2 rel), widened by 4 u for the products' own rounding */
+        const float lo = t * (1.0f - 2.0f * rel - 4.0f * TBF_U), hi = t * (1.0f + 2.0f * rel + 4.0f * TBF_U);
+        if (lo > 0.050001f && hi < u->best0_lo)
             ground = 1;
-            best_lo = lo;
-            best_hi = hi;
-        } else if (!(hi < 0.05 || lo > u->best0)) {
+        else if (!(hi < 0.049999f || lo > u->best0_hi))
             return 0; /* too close to call: the double trace decides */
-        }
     } else if (!(dz > -1e-5f + TBF_ED)) {
         return 0;
     }
-    /* the dome is tested after the spheres (all missed) and before the balls
-     * (in the sphere list, all missed): it wins when td > 0.05 and td < best */
-    int dome = 0;
-    float td = 0.0f, etd = 0.0f;
-    if (u->dome) {
-        const int d = tbf_dome(u, dx, dy, &td, &etd);
-        if (d < 0) return 0;
-        if (d > 0) {
-            const double lo = (double)td - etd, hi = (double)td + etd;
-            if (lo > 0.05 && hi < best_lo)
-                dome = 1;
-            else if (!(hi < 0.05 || lo > best_hi))
-                return 0;
-        }
-    }
     float x, m;
-    if (dome) {
-        const float e = TBF_EXPF(td * -0.0125f);
-        x = 0.46f * (0.75f + 0.25f * e) * 255.0f;
-        m = 255.0f * (0.46f * 0.25f * (e + 1e-6f) * (etd + 3.0f * TBF_U * td) * 0.0125f + 6e-7f);
-    } else if (ground) {
+    if (ground) {
         const float luma = 0.28f + 0.17f * fminf(1.0f, fmaxf(0.0f, -dz));
         const float e = TBF_EXPF(t * -0.0125f);
         x = luma * (0.75f + 0.25f * e) * 255.0f;
