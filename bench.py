@@ -71,6 +71,10 @@ def parse_args():
     p.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed outputs")
     p.add_argument("--config1-only", action="store_true",
                    help="run only the config-1 latency leg (one GPU) and print its JSON")
+    p.add_argument("--actor-inputs-only", action="store_true",
+                   help="run only the learner-input entry point on --batch aircraft (one GPU) and print its JSON")
+    p.add_argument("--all-scanning", action="store_true",
+                   help="with --actor-inputs-only: every mission reads the LiDAR scans (half dodge, half slalom)")
     return p.parse_args()
 
 
@@ -283,6 +287,40 @@ def profiled_sensor_pipes():
     except (OSError, ValueError):
         pass
     return out
+
+
+def time_actor_inputs_only(args, dev):
+    """tb_cuda_prepare_actor_inputs_device alone on --batch aircraft of the
+    seeded batch (the missions as generated, or with --all-scanning half
+    dodge and half slalom): W warm-up calls, then K calls between one CUDA
+    event pair on the launching stream.  A small command for profilers."""
+    import torch
+
+    n = args.batch
+    obs, mission, cams, _ = tb.generate(SEED, 0, n, total=n, pinned=True)
+    if args.all_scanning:
+        mission = np.array(mission, copy=True)
+        mission[0::2, 5] = 1.0
+        mission[1::2, 4] = 1.0
+        mission[1::2, 5] = -0.5
+    d_obs, d_mis, d_cam = (torch.from_numpy(np.ascontiguousarray(x)).to(dev) for x in (obs, mission, cams))
+    shapes = ((n, 91), (n, 49), (n, 24), (n, 15), (n, 6 * 2048), (n, 16384))
+    outs = [torch.empty(sh, dtype=torch.float32, device=dev) for sh in shapes]
+    stream = torch.cuda.Stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        assert tb.tb_cuda_prepare_actor_inputs_device(d_obs, d_mis, d_cam, *outs, n, stream) == 1
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        tb.tb_cuda_prepare_actor_inputs_device(d_obs, d_mis, d_cam, *outs, n, stream)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    assert tb.tb_cuda_synchronize(stream) == 1
+    ms = start.elapsed_time(end) / args.steps
+    return {"leg": "actor_inputs", "entry_point": "tb_cuda_prepare_actor_inputs_device", "aircraft": n,
+            "missions": "all scanning" if args.all_scanning else "as generated", "steps": args.steps,
+            "ms_per_call": ms, "launches_per_call": 2}
 
 
 def time_config1(stream, dev):
@@ -909,7 +947,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                  "bytes_per_sample": bpa,
                  "roofline": {"bound": "hbm (78 % writes)", "achieved": a_ach, "peak": peak_gbs, "unit": "GB/s",
                               "frac": a_ach / peak_gbs, "peak_source": f"{peak_kind} hbm_gbs (copy)"},
-                 "launches": 3 * a_steps}  # onboard scan + control, then the streaming kernel
+                 "launches": 2 * a_steps}  # the streaming kernel (with the scans), then the control law
         del a_outs
         torch.cuda.empty_cache()
 
@@ -1218,6 +1256,14 @@ def main():
         tb.load_library()
         if rank == 0:
             print(json.dumps(time_config1(torch.cuda.Stream(), torch.device("cuda", local_rank))), flush=True)
+        return
+    if args.actor_inputs_only:
+        import torch
+
+        torch.cuda.set_device(local_rank)
+        tb.load_library()
+        if rank == 0:
+            print(json.dumps(time_actor_inputs_only(args, torch.device("cuda", local_rank))), flush=True)
         return
     if world > 1:
         import datetime

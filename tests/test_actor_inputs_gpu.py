@@ -20,6 +20,7 @@ import pytest
 import oracle
 import turbinator_c_b200 as tb
 from tests.golden import fixtures
+from tests.onboard_cases import cluster_cancellation, force_modes
 
 torch = pytest.importorskip("torch")
 
@@ -43,7 +44,7 @@ def run(obs, mission, cams):
     return d, [o.cpu().numpy() for o in outs]
 
 
-def check(obs, mission, cams, what):
+def check(obs, mission, cams, what, ref_onboard=True):
     d, (proprio, mvec, tac, pri, lidar, luma) = run(obs, mission, cams)
     n = obs.shape[0]
     for a in (proprio, mvec, tac, pri, lidar, luma):
@@ -68,11 +69,12 @@ def check(obs, mission, cams, what):
         assert np.array_equal(luma.view(np.uint32), rlu.view(np.uint32)), what
         assert np.array_equal(proprio[:, :52].view(np.uint32), rp[:, :52].view(np.uint32)), what
         assert np.array_equal(mvec[:, :10].view(np.uint32), rm[:, :10].view(np.uint32)), what
-        mine = np.concatenate([tac, pri], 1)
-        theirs = np.concatenate([rt, rpri], 1)
-        assert np.max(np.abs(mine.astype(np.float64) - theirs)) <= 5e-5, what
-        for c in FLAGS_TACTICAL + (24 + 14,):
-            assert np.array_equal(mine[:, c], theirs[:, c]), what
+        if ref_onboard:
+            mine = np.concatenate([tac, pri], 1)
+            theirs = np.concatenate([rt, rpri], 1)
+            assert np.max(np.abs(mine.astype(np.float64) - theirs)) <= 5e-5, what
+            for c in FLAGS_TACTICAL + (24 + 14,):
+                assert np.array_equal(mine[:, c], theirs[:, c]), what
 
 
 def test_seeded_batch():
@@ -121,6 +123,52 @@ def test_bounded_pipeline_wait_reports_and_recovers():
     assert tb.tb_cuda_synchronize() == 0
     assert tb.tb_cuda_synchronize() == 1          # reported once, then cleared
     check(obs, mission, cams, "after-timeout")
+
+
+def test_bounded_wait_in_scan_mode_reports_and_recovers():
+    """The same with the kernel scanning the LiDAR rows it stages (all
+    consumer warps take part in every scan): the withheld aircraft is a dodge
+    aircraft; every consumer warp leaves at the expired wait, the launch ends,
+    the timeout is reported once, and the next call is whole and correct."""
+    n = 64
+    obs, mission, cams, _ = tb.generate(46, 0, n)
+    mission = mission.copy()
+    rows = np.arange(n)
+    force_modes(mission, rows[0::2], rows[1::2])
+    d = [torch.from_numpy(x).cuda() for x in (obs, mission, cams)]
+    outs = _outputs(n)
+    assert tb.take_status() == 0 and tb.tb_cuda_synchronize() == 1
+    assert tb.launch_actor_inputs_scan(*d, outs[3], outs[0], outs[1], outs[4], outs[5], n, None,
+                                       wait_ns=20_000_000, stall_sample=6) == 1
+    assert tb.tb_cuda_synchronize() == 0
+    assert tb.tb_cuda_synchronize() == 1          # reported once, then cleared
+    check(obs, mission, cams, "after-scan-timeout")
+
+
+@pytest.mark.parametrize("stress", [False, True])
+def test_every_aircraft_scans(stress):
+    """Every aircraft's mission reads the LiDAR scans, which the streaming
+    kernel runs from its staged rows: half dodge (nearest return; first-index
+    ties in stress quarter (c)), half slalom (corridor minimum, cluster count
+    and cluster sign)."""
+    n = 8192
+    obs, mission, cams, _ = tb.generate(4, 0, n, total=n, stress=stress)
+    rows = np.arange(n)
+    force_modes(mission, rows[0::2], rows[1::2])
+    obs[:, 2] = 9.0
+    check(obs, mission, cams, f"scans/stress={stress}")
+
+
+def test_cluster_sign_near_cancellation():
+    """Mirror-symmetric corridor returns: the sign of the cluster y sum
+    needs the reference's in-order float sum, which the kernel's warp 0 forms
+    when the double sum and its bound cannot decide.  The onboard values are
+    held to the correctly rounded build exactly; not to the reference's GPU
+    build, which contracts the products of each y into multiply-adds and so
+    finds its own sign for sums that cancel to rounding level."""
+    obs, mission = cluster_cancellation(1024)
+    cams = np.zeros((obs.shape[0], 16384), np.uint8)
+    check(obs, mission, cams, "cluster-sign", ref_onboard=False)
 
 
 @pytest.mark.skipif(not oracle.have_reference_actor_inputs(), reason="reference GPU build absent")

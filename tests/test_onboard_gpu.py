@@ -27,6 +27,7 @@ import pytest
 import oracle
 import turbinator_c_b200 as tb
 from tests.golden import fixtures
+from tests.onboard_cases import cluster_cancellation, force_modes
 
 torch = pytest.importorskip("torch")
 
@@ -127,7 +128,7 @@ def test_config2_full(scanning):
     name = "config2"
     if scanning:
         rows = np.arange(batch)
-        _force_modes(mission, rows[0::2], rows[1::2])
+        force_modes(mission, rows[0::2], rows[1::2])
         name = "config2_all_scanning"
     stats = check_onboard(run_onboard(obs, mission), obs, mission, name)
     check_config_deviation(stats, name)
@@ -181,12 +182,6 @@ def test_argument_rejection():
     assert tb.tb_cuda_extract_onboard_device(d.data_ptr() + 2, d, d, d, 1) == 0
 
 
-def _force_modes(mission, dodge_rows, slalom_rows):
-    mission[dodge_rows, 5] = 1.0          # dodge: nearest-return avoidance
-    mission[slalom_rows, 4] = 1.0         # slalom (with m[5] <= 0.25): corridor cluster
-    mission[slalom_rows, 5] = -0.5
-
-
 @pytest.mark.parametrize("stress", [False, True])
 def test_every_aircraft_scans(stress):
     """Missions that read the LiDAR scans for every aircraft: half dodge
@@ -195,7 +190,7 @@ def test_every_aircraft_scans(stress):
     n = 32768
     obs, mission, _, _ = tb.generate(4, 0, n, stress=stress)
     rows = np.arange(n)
-    _force_modes(mission, rows[0::2], rows[1::2])
+    force_modes(mission, rows[0::2], rows[1::2])
     obs[:, 2] = 9.0
     check_onboard(run_onboard(obs, mission), obs, mission, f"scans/stress={stress}")
 
@@ -204,30 +199,7 @@ def test_cluster_sign_near_cancellation():
     """Mirror-symmetric corridor returns make the cluster y sum cancel to
     rounding level, so its sign cannot be read off a reordered sum: the
     kernel must fall back to the reference's in-order float sum."""
-    rng = np.random.default_rng(11)
-    n = 2048
-    obs = np.zeros((n, 4148), np.float32)
-    mission = np.zeros((n, 10), np.float32)
-    obs[:, 6] = 1.0                                   # level attitude
-    obs[:, 2] = 9.0
-    obs[:, 1] = 0.0                                   # on the lane centre line
-    obs[:, 40] = 0.5
-    mission[:, 4] = 1.0                               # slalom
-    mission[:, 7:10] = rng.uniform(-0.5, 0.5, (n, 3)).astype(np.float32)
-    lidar = np.full((n, 2, 16, 128), 50.0, np.float32)  # out of the 0.35-11.5 m window
-    for i in range(n):
-        k = int(rng.integers(1, 16))                   # forward azimuth index and its mirror 96 - k
-        r = np.float32(rng.uniform(1.0, 2.5))
-        el = int(rng.integers(0, 3))
-        lidar[i, 0, el, k] = r
-        lidar[i, 0, el, 96 - k] = r
-        if i % 3 == 0:                                 # a second symmetric pair
-            k2 = int(rng.integers(1, 16))
-            lidar[i, 1, el, k2] = r
-            lidar[i, 1, el, 96 - k2] = r
-        if i % 5 == 0:                                 # tiny attitude tilt: near, not exact, symmetry
-            obs[i, 9] = np.float32(rng.uniform(-1e-6, 1e-6))
-    obs[:, 48:4144] = lidar.reshape(n, 4096)
+    obs, mission = cluster_cancellation(2048)
     out = run_onboard(obs, mission)
     check_onboard(out, obs, mission, "cluster-sign")
 

@@ -98,6 +98,7 @@ def load_library() -> ctypes.CDLL:
           [_c.c_int, _c.POINTER(_c.c_int)] + [_c.POINTER(_vp)] * 4 + [_c.POINTER(_sz), _c.POINTER(_vp)])
     _bind(lib, "tb_onboard_launch", _c.c_int, [_vp] * 4 + [_sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_actor_inputs_launch", _c.c_int, [_vp] * 9 + [_sz, _vp, _c.POINTER(LaunchOpts)])
+    _bind(lib, "tb_actor_inputs_scan_launch", _c.c_int, [_vp] * 8 + [_sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_launch_f32cam", _c.c_int,
           [_vp, _vp, _vp, _vp, _sz, _vp, _c.POINTER(LaunchOpts)])
     _bind(lib, "tb_features_launch", _c.c_int,
@@ -247,6 +248,17 @@ def launch_actor_inputs(obs, mission, cameras, tactical, prior, proprio, mission
     return load_library().tb_actor_inputs_launch(
         _ptr(obs), _ptr(mission), _ptr(cameras), _ptr(tactical), _ptr(prior), _ptr(proprio), _ptr(mission_vec),
         _ptr(lidar), _ptr(luma), batch_size, _stream_handle(stream), _c.byref(opts))
+
+
+def launch_actor_inputs_scan(obs, mission, cameras, prior, proprio, mission_vec, lidar, luma, batch_size: int,
+                             stream=None, *, wait_ns: int = 0, stall_sample: int = -1) -> int:
+    """The learner-input streaming kernel as the learner-input entry point
+    launches it (it also scans the LiDAR rows of the dodge and slalom aircraft
+    and parks the results in `prior`); test hook: bounded waits."""
+    opts = LaunchOpts(0, 0, wait_ns, stall_sample, 0)
+    return load_library().tb_actor_inputs_scan_launch(
+        _ptr(obs), _ptr(mission), _ptr(cameras), _ptr(prior), _ptr(proprio), _ptr(mission_vec), _ptr(lidar),
+        _ptr(luma), batch_size, _stream_handle(stream), _c.byref(opts))
 
 
 def take_status(stream=None) -> int:

@@ -47,6 +47,7 @@
 #include <stdint.h>
 
 #include "tb_features_internal.h"
+#include "tb_onboard_scan.cuh"
 #include "tb_pipeline.cuh"
 #include "turbinator/training/cuda_features.h"
 
@@ -76,8 +77,14 @@ constexpr uint32_t kStageBytes = (kPriorOff + 15 * 4 + 127) / 128 * 128;
 constexpr int kStages = 3;
 constexpr unsigned long long kMaxChunk = 2; /* aircraft per CTA */
 constexpr uint32_t kBarrierRegion = 128;
-constexpr uint32_t kSmemBytes = kBarrierRegion + kStages * kStageBytes;
+/* After the ring: the scans' ray tables and per-warp partial results (about
+ * 1.5 KB), used in scan mode. */
+using ScanShared = tb_scan::BlockScanShared<kConsumerWarps>;
+constexpr uint32_t kScanOff = kBarrierRegion + kStages * kStageBytes;
+constexpr uint32_t kSmemBytes = kScanOff + (sizeof(ScanShared) + 15) / 16 * 16;
 static_assert(kObsBytes % 16 == 0 && kCameraBytes % 16 == 0 && kStageBytes == 33280, "stage layout");
+static_assert(2 * (kSmemBytes + 1024) <= 228 * 1024, "two CTAs per SM");
+constexpr int kScanBarrier = 1; /* named barrier of the 256 consumer threads */
 
 constexpr unsigned long long kDefaultWaitNs = 1000000000ull; /* ~1 s per wait */
 
@@ -126,7 +133,38 @@ struct ActorArgs {
     unsigned long long wait_ns;
     long long stall_sample; /* test hook: withhold this aircraft's copies; -1 normally */
     unsigned int *status;   /* the launching stream's status word */
+    int scan;               /* 0: copy the staged tactical / prior rows into the onboard columns;
+                               1: scan the dodge / slalom aircraft's LiDAR rows, park the results in
+                               `park` (the prior rows) and leave the onboard columns to the
+                               control-law kernel */
+    float *park;
 };
+
+/* All 256 consumer threads vote; every one of them gets the AND.  Every
+ * consumer reaches it once per staged aircraft (after its own bounded wait),
+ * so a wait that expired in one warp makes all of them leave together and no
+ * consumer is left at a later barrier. */
+__device__ __forceinline__ bool consumers_all(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(ok)), "n"(kScanBarrier), "n"(kConsumers)
+        : "memory");
+    return r != 0;
+}
+
+/* Sanitised mission value: NaN -> 0, +-inf -> +-1 (onboard_features.cuh:12-14). */
+__device__ __forceinline__ float mission_sane(float x) {
+    return isnan(x) ? 0.0f : (isinf(x) ? copysignf(1.0f, x) : x);
+}
+/* Sanitised observation value: NaN -> 0, +-inf -> +-1000. */
+__device__ __forceinline__ float obs_sane(float x) {
+    return isnan(x) ? 0.0f : (isinf(x) ? copysignf(1000.0f, x) : x);
+}
 
 __global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -165,8 +203,10 @@ __global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorAr
             const uint32_t stage = smem_addr(stages + static_cast<size_t>(s) * kStageBytes);
             /* the 4-byte-aligned rows: mission, tactical, prior (49 floats) */
             if (lane < kMissionDim) async_load4(stage + kMissionOff + 4 * lane, a.mission + b * kMissionDim + lane);
-            if (lane < 24) async_load4(stage + kTacticalOff + 4 * lane, a.tactical + b * 24 + lane);
-            if (lane < 15) async_load4(stage + kPriorOff + 4 * lane, a.prior + b * 15 + lane);
+            if (!a.scan) {
+                if (lane < 24) async_load4(stage + kTacticalOff + 4 * lane, a.tactical + b * 24 + lane);
+                if (lane < 15) async_load4(stage + kPriorOff + 4 * lane, a.prior + b * 15 + lane);
+            }
             if (lane < 24) async_track(full_bar + 8 * s);
             __syncwarp();
             if (lane == 0) {
@@ -188,11 +228,15 @@ __global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorAr
 
     /* ---------------- consumer warps ---------------- */
     const int t = threadIdx.x; /* 0..255 */
+    ScanShared &scan_sh = *reinterpret_cast<ScanShared *>(smem + kScanOff);
+    if (a.scan) tb_scan::load_tables(scan_sh.tables, t, kConsumers); /* visible after the first vote */
     unsigned long long k = 0;
     for (unsigned long long b = first; b < last; ++b, ++k) {
         const int s = static_cast<int>(k % kStages);
         const uint32_t phase = static_cast<uint32_t>((k / kStages) & 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(full_bar + 8 * s, phase, a.wait_ns))) {
+        bool ok = __all_sync(0xffffffffu, mbar_wait(full_bar + 8 * s, phase, a.wait_ns));
+        if (a.scan) ok = consumers_all(ok); /* the scan below synchronises all consumer warps */
+        if (!ok) {
             if (lane == 0) atomicOr(a.status, TB_FEATURE_STATUS_WAIT_TIMEOUT);
             return;
         }
@@ -237,6 +281,8 @@ __global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorAr
         } else if (t < 52 + kMissionDim) {
             const float mm = m[t - 52];
             mv[t - 52] = isfinite(mm) ? mm : 0.0f;
+        } else if (a.scan) {
+            /* the control-law kernel writes the onboard columns */
         } else if (t >= 64 && t < 64 + 24) {
             const float v = reinterpret_cast<const float *>(stage + kTacticalOff)[t - 64];
             p[52 + (t - 64)] = v;
@@ -245,6 +291,23 @@ __global__ void __launch_bounds__(kThreads, 2) actor_inputs_kernel(const ActorAr
             const float v = reinterpret_cast<const float *>(stage + kPriorOff)[t - 96];
             p[76 + (t - 96)] = v;
             mv[34 + (t - 96)] = v;
+        }
+
+        /* Onboard LiDAR scans of a dodge or slalom aircraft (onboard_features.cuh:
+         * 185-239) from its staged row, by all consumer warps; the results
+         * go to the first six floats of its prior row for the control law. */
+        if (a.scan) {
+            const float m4 = mission_sane(m[4]), m5 = mission_sane(m[5]);
+            const bool dodge = m5 > 0.75f;
+            const bool slalom = m4 > 0.75f && !(m4 > 0.75f && m5 > 0.25f);
+            if (dodge || slalom) { /* the same in every consumer thread */
+                const tb_scan::Attitude at =
+                    tb_scan::attitude_from(obs_sane(o[6]), obs_sane(o[7]), obs_sane(o[8]), obs_sane(o[9]));
+                const tb_scan::RayStats st =
+                    tb_scan::block_scan<kConsumerWarps>(scan_sh, o + 48, o + 48 + kLidarBins, at, obs_sane(o[1]),
+                                                        dodge, slalom, warp, lane, kScanBarrier);
+                if (t == 0) tb_scan::park_stats(a.park + b * 15, st);
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar + 8 * s);
@@ -258,12 +321,11 @@ bool aligned(const void *p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p
 
 } /* namespace */
 
-/* Launches the streaming kernel alone (tactical and prior already computed);
- * opts may be NULL (its wait_ns and stall_sample fields are honoured). */
-extern "C" int tb_actor_inputs_launch(const float *obs, const float *mission, const unsigned char *cameras,
-                                      const float *tactical, const float *prior, float *proprio,
-                                      float *mission_vec, float *lidar, float *luma, size_t batch, void *stream,
-                                      const tb_features_launch_opts *opts) {
+/* Launches the streaming kernel; opts may be NULL (its wait_ns and
+ * stall_sample fields are honoured).  scan selects the mode (ActorArgs). */
+static int actor_launch(const float *obs, const float *mission, const unsigned char *cameras, const float *tactical,
+                        const float *prior, float *proprio, float *mission_vec, float *lidar, float *luma,
+                        size_t batch, void *stream, const tb_features_launch_opts *opts, float *park) {
     if (batch == 0 || batch > 0x7fffffffu) return 0;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
@@ -292,6 +354,8 @@ extern "C" int tb_actor_inputs_launch(const float *obs, const float *mission, co
     a.stall_sample = opts ? opts->stall_sample : -1;
     a.status = tb_status_slot(stream);
     if (!a.status) return 0;
+    a.scan = park != nullptr;
+    a.park = park;
     cudaGetLastError(); /* report this launch only */
     /* runs of up to kMaxChunk aircraft, but no fewer CTAs than fit at once */
     const unsigned long long resident = static_cast<unsigned long long>(g_resident[dev]);
@@ -300,6 +364,24 @@ extern "C" int tb_actor_inputs_launch(const float *obs, const float *mission, co
     const unsigned long long grid = (batch + a.chunk - 1) / a.chunk;
     actor_inputs_kernel<<<static_cast<unsigned int>(grid), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(a);
     return cudaGetLastError() == cudaSuccess;
+}
+
+extern "C" int tb_actor_inputs_launch(const float *obs, const float *mission, const unsigned char *cameras,
+                                      const float *tactical, const float *prior, float *proprio,
+                                      float *mission_vec, float *lidar, float *luma, size_t batch, void *stream,
+                                      const tb_features_launch_opts *opts) {
+    if (!tactical || !prior) return 0;
+    return actor_launch(obs, mission, cameras, tactical, prior, proprio, mission_vec, lidar, luma, batch, stream,
+                        opts, nullptr);
+}
+
+extern "C" int tb_actor_inputs_scan_launch(const float *obs, const float *mission, const unsigned char *cameras,
+                                           float *prior, float *proprio, float *mission_vec, float *lidar,
+                                           float *luma, size_t batch, void *stream,
+                                           const tb_features_launch_opts *opts) {
+    if (!prior) return 0;
+    return actor_launch(obs, mission, cameras, nullptr, nullptr, proprio, mission_vec, lidar, luma, batch, stream,
+                        opts, prior);
 }
 
 extern "C" int tb_cuda_prepare_actor_inputs_device(const float *device_obs, const float *device_mission,
@@ -316,10 +398,14 @@ extern "C" int tb_cuda_prepare_actor_inputs_device(const float *device_obs, cons
         !aligned(device_camera_luma, 16) || !aligned(device_mission, 4) || !aligned(device_proprio_91, 4) ||
         !aligned(device_mission_49, 4))
         return 0;
-    if (!tb_cuda_extract_onboard_device(device_obs, device_mission, device_tactical_24, device_prior_15,
-                                        batch_size, stream))
+    /* One pass over the staged rows (learner tensors, and the LiDAR scans of
+     * the dodge and slalom aircraft parked in their prior rows), then the
+     * control law, which writes tactical, prior and the onboard columns of
+     * the proprio and mission rows. */
+    if (!tb_actor_inputs_scan_launch(device_obs, device_mission, device_cameras, device_prior_15, device_proprio_91,
+                                     device_mission_49, device_lidar_6x2048, device_camera_luma, batch_size, stream,
+                                     nullptr))
         return 0;
-    return tb_actor_inputs_launch(device_obs, device_mission, device_cameras, device_tactical_24, device_prior_15,
-                                  device_proprio_91, device_mission_49, device_lidar_6x2048, device_camera_luma,
-                                  batch_size, stream, nullptr);
+    return tb_onboard_control_launch(device_obs, device_mission, device_tactical_24, device_prior_15, batch_size,
+                                     stream, device_proprio_91, device_mission_49);
 }

@@ -25,8 +25,9 @@
  *    one aircraft per thread without shared memory (onboard_control_kernel),
  *    so a 65,536-aircraft batch is one wave; a scanned aircraft's results
  *    reach it parked in its own prior row.
- *  - Ray directions (12 elevation and 128 azimuth cosines/sines) are built
- *    once per CTA in shared memory.
+ *  - Ray directions (12 elevation and 128 azimuth cosines/sines, correctly
+ *    rounded constants in tb_scan_tables.h) are copied once per CTA into
+ *    shared memory.
  *
  * Arithmetic: this file is compiled with -fmad=false, so every float
  * multiply and add rounds separately in the reference's expression order, as
@@ -43,6 +44,7 @@
 #include <stdint.h>
 
 #include "tb_features_internal.h"
+#include "tb_onboard_scan.cuh"
 #include "tb_pipeline.cuh"
 #include "turbinator/training/cuda_features.h"
 
@@ -72,6 +74,7 @@ __device__ __noinline__ double d_tanh(double x) { return tanh(x); }
 __device__ __noinline__ double d_exp(double x) { return exp(x); }
 __device__ __noinline__ double d_atan2(double y, double x) { return atan2(y, x); }
 __device__ __noinline__ double d_hypot(double x, double y) { return hypot(x, y); }
+__device__ __noinline__ void d_sincos(double x, double *s, double *c) { sincos(x, s, c); }
 __device__ __forceinline__ float cr_sin(float x) { return static_cast<float>(d_sin(static_cast<double>(x))); }
 __device__ __forceinline__ float cr_cos(float x) { return static_cast<float>(d_cos(static_cast<double>(x))); }
 __device__ __forceinline__ float cr_tan(float x) { return static_cast<float>(d_tan(static_cast<double>(x))); }
@@ -82,6 +85,13 @@ __device__ __forceinline__ float cr_tanh(float x) { return static_cast<float>(d_
 __device__ __forceinline__ float cr_exp(float x) { return static_cast<float>(d_exp(static_cast<double>(x))); }
 __device__ __forceinline__ float cr_atan2(float y, float x) {
     return static_cast<float>(d_atan2(static_cast<double>(y), static_cast<double>(x)));
+}
+/* sin and cos of one argument from one call (one range reduction). */
+__device__ __forceinline__ void cr_sincos(float x, float &s, float &c) {
+    double ds, dc;
+    d_sincos(static_cast<double>(x), &ds, &dc);
+    s = static_cast<float>(ds);
+    c = static_cast<float>(dc);
 }
 __device__ __forceinline__ float cr_hypot(float x, float y) {
     return static_cast<float>(d_hypot(static_cast<double>(x), static_cast<double>(y)));
@@ -105,7 +115,9 @@ __device__ __forceinline__ float mission_value(float x) {
 /* Angle difference wrapped through atan2(sin, cos). */
 __device__ __forceinline__ float wrap(float target, float current) {
     const float d = target - current;
-    return cr_atan2(cr_sin(d), cr_cos(d));
+    float s, c;
+    cr_sincos(d, s, c);
+    return cr_atan2(s, c);
 }
 __device__ __forceinline__ float norm3(float x, float y, float z) { return sqrtf(x * x + y * y + z * z); }
 /* Final tactical sanitiser: NaN -> 0, +-inf -> +-1. */
@@ -113,67 +125,15 @@ __device__ __forceinline__ float unit_sane(float x) {
     return isnan(x) ? 0.0f : (isinf(x) ? copysignf(1.0f, x) : x);
 }
 
-/* Per-aircraft summary of the two LiDAR passes (onboard_features.cuh:185-234). */
-struct RayStats {
-    float min_r, min_r_dx, min_r_dy;  /* nearest return in elevations 0..3 and its world x, y */
-    float min_dx_c;                   /* nearest obstacle centre ahead inside the corridor */
-    float cluster_y_sum;              /* sum of corridor centres' y within 1.4 m of min_dx_c, or a
-                                         value of the same sign (only its sign is read) */
-    int cluster_count;
-};
-
-/* Body-to-world rotation of the normalised attitude quaternion, as the
- * prior forms it (onboard_features.cuh:104-137). */
-struct Attitude {
-    float qw, qx, qy, qz;
-    float r00, r01, r02, r10, r11, r12, r20, r21, r22;
-};
-
-__device__ __forceinline__ Attitude attitude_from(const float o6, const float o7, const float o8,
-                                                  const float o9) {
-    Attitude a;
-    float qnorm = fmaxf(norm3(o6, o7, o8), 0.0f);
-    qnorm = fmaxf(sqrtf(qnorm * qnorm + o9 * o9), 1.0e-8f);
-    const float sign = o6 < 0.0f ? -1.0f : 1.0f;
-    a.qw = sign * o6 / qnorm;
-    a.qx = sign * o7 / qnorm;
-    a.qy = sign * o8 / qnorm;
-    a.qz = sign * o9 / qnorm;
-    const float qw = a.qw, qx = a.qx, qy = a.qy, qz = a.qz;
-    a.r00 = 1.0f - 2.0f * (qy * qy + qz * qz);
-    a.r01 = 2.0f * (qx * qy - qw * qz);
-    a.r02 = 2.0f * (qx * qz + qw * qy);
-    a.r10 = 2.0f * (qx * qy + qw * qz);
-    a.r11 = 1.0f - 2.0f * (qx * qx + qz * qz);
-    a.r12 = 2.0f * (qy * qz - qw * qx);
-    a.r20 = 2.0f * (qx * qz - qw * qy);
-    a.r21 = 2.0f * (qy * qz + qw * qx);
-    a.r22 = 1.0f - 2.0f * (qx * qx + qy * qy);
-    return a;
-}
-
-/* Shared per-CTA ray direction tables. */
-struct RayTables {
-    float cos_el[12], sin_el[12];     /* index head * 6 + el */
-    float cos_az[128], sin_az[128];
-};
-
-__device__ void build_ray_tables(RayTables &t) {
-    const float pi = 3.14159265358979323846f;
-    for (int i = threadIdx.x; i < 12 + 128; i += blockDim.x) {
-        if (i < 12) {
-            const int head = i / 6, el = i % 6;
-            const float elev = (head == 0 ? 1.0f : -1.0f) * (pi * static_cast<float>(el) / 30.0f);
-            t.cos_el[i] = cr_cos(elev);
-            t.sin_el[i] = cr_sin(elev);
-        } else {
-            const int azi = i - 12;
-            const float azim = pi * (0.25f + static_cast<float>(azi) / 64.0f);
-            t.cos_az[azi] = cr_cos(azim);
-            t.sin_az[azi] = cr_sin(azim);
-        }
-    }
-}
+/* The scan summary, its parked form, the attitude rotation and the ray
+ * direction tables are shared with the learner-input kernel
+ * (tb_onboard_scan.cuh). */
+using tb_scan::Attitude;
+using tb_scan::RayStats;
+using tb_scan::RayTables;
+using tb_scan::attitude_from;
+using tb_scan::park_stats;
+using tb_scan::unpark_stats;
 
 /* Per-warp shared memory: one staged LiDAR block (the 1,536 controller rays
  * of one aircraft, in ray order) and pass 1's corridor-centre x per ray (+inf
@@ -295,13 +255,7 @@ __device__ RayStats scan_rays(const RayTables &t, WarpSlot &slot, const float *r
         }
     }
 
-    RayStats s;
-    s.min_r = 30.0f;
-    s.min_r_dx = 0.0f;
-    s.min_r_dy = 0.0f;
-    s.min_dx_c = 30.0f;
-    s.cluster_count = 0;
-    s.cluster_y_sum = 0.0f;
+    RayStats s = tb_scan::initial_stats();
     if (want_near) {
         const float lane_wx = near_wx, lane_wy = near_wy;
         warp_argmin(near_r, near_ray);
@@ -399,7 +353,9 @@ __device__ void tactical(const float *o, const float *m, float *out) {
     const float ct = nclamp(1.0f - 2.0f * (qx * qx + qy * qy), -1.0f, 1.0f);
     const float bx_x = 1.0f - 2.0f * (qy * qy + qz * qz);
     const float bx_y = 2.0f * (qx * qy + qw * qz);
-    const float yaw = cr_atan2(bx_y, bx_x), cy = cr_cos(yaw), sy = cr_sin(yaw);
+    const float yaw = cr_atan2(bx_y, bx_x);
+    float sy, cy;
+    cr_sincos(yaw, sy, cy);
     t[8] = cy * bz_y - sy * bz_x;
     t[9] = -sy * bz_y - cy * bz_x;
     t[10] = ct;
@@ -463,8 +419,11 @@ __device__ void prior(const float *o, const float *m, const RayStats &rs, float 
         thrust[i] = max_installed * (idle_frac + (1.0f - idle_frac) * spool[i]);
         outer[i] = cr_atan2(o[20 + i], o[24 + i]);
         const float inner = o[28 + i];
-        fz[i] = thrust[i] * cr_cos(outer[i]) * cr_cos(inner);
-        ft[i] = thrust[i] * cr_sin(outer[i]) * cr_cos(inner);
+        float so, co;
+        cr_sincos(outer[i], so, co);
+        const float ci = cr_cos(inner);
+        fz[i] = thrust[i] * co * ci;
+        ft[i] = thrust[i] * so * ci;
         total_fz += fz[i];
         jammed_yaw_ft += ft[i];
     }
@@ -533,8 +492,10 @@ __device__ void prior(const float *o, const float *m, const RayStats &rs, float 
     float avoid_x = 0.0f, avoid_y = 0.0f, slalom_speed = 3.8f, nearest_dx = 30.0f;
     if (dodge && rs.min_r < 7.5f) {
         const float min_az = cr_atan2(rs.min_r_dy, rs.min_r_dx);
-        avoid_x = -cr_sin(min_az) * 2.2f;
-        avoid_y = cr_cos(min_az) * 2.2f;
+        float sa, ca;
+        cr_sincos(min_az, sa, ca);
+        avoid_x = -sa * 2.2f;
+        avoid_y = ca * 2.2f;
     }
     const float min_dx_c = rs.min_dx_c;
     const float cluster_y = rs.cluster_y_sum / fmaxf(static_cast<float>(rs.cluster_count), 1.0f);
@@ -628,7 +589,8 @@ __device__ void prior(const float *o, const float *m, const RayStats &rs, float 
     const float damp_v = active_slalom ? 0.8f : 0.4f;
     const float fx_world = (mass * des_ax + damp_v * vx - tilt_comp * total_fz * body_z_x) * horiz_scale;
     const float fy_world = (mass * des_ay + damp_v * vy - tilt_comp * total_fz * body_z_y) * horiz_scale;
-    const float cyw = cr_cos(yaw), syw = cr_sin(yaw);
+    float syw, cyw;
+    cr_sincos(yaw, syw, cyw);
     const float max_fh = active_slalom ? 105.0f : (lateral ? 125.0f : (heavy_cargo ? 52.0f : 80.0f));
     const float fx_body = nclamp(cyw * fx_world + syw * fy_world, -max_fh, max_fh);
     const float fy_body = nclamp(-syw * fx_world + cyw * fy_world, -max_fh, max_fh);
@@ -775,7 +737,8 @@ __device__ void prior(const float *o, const float *m, const RayStats &rs, float 
         const float pitch_up = cr_asin(nclamp(r20, -1.0f, 1.0f));
         const float climb_des = nclamp(0.42f * gz, -5.0f, 5.0f);
         const float climb_err = climb_des - vz;
-        const float cos_bank = cr_cos(roll_right), sin_bank = cr_sin(roll_right);
+        float sin_bank, cos_bank;
+        cr_sincos(roll_right, sin_bank, cos_bank);
         const float gamma_des = cr_atan2(climb_des, fmaxf(gs, 14.0f));
         float desired_pitch = nclamp(0.062831853f + 0.75f * gamma_des +
             0.035f * climb_err + 0.09f * (1.0f - fmaxf(cos_bank, 0.5f)), -0.15f, 0.25f);
@@ -845,27 +808,6 @@ __device__ __forceinline__ void scan_modes(const float *mrow, bool &dodge, bool 
     slalom = m4 > 0.75f && !(m4 > 0.75f && m5 > 0.25f);
 }
 
-/* RayStats parked in a prior row between the two launches (24 of its 60 bytes). */
-__device__ __forceinline__ void park_stats(float *row, const RayStats &st) {
-    row[0] = st.min_r;
-    row[1] = st.min_r_dx;
-    row[2] = st.min_r_dy;
-    row[3] = st.min_dx_c;
-    row[4] = st.cluster_y_sum;
-    row[5] = __int_as_float(st.cluster_count);
-}
-
-__device__ __forceinline__ RayStats unpark_stats(const float *row) {
-    RayStats st;
-    st.min_r = row[0];
-    st.min_r_dx = row[1];
-    st.min_r_dy = row[2];
-    st.min_dx_c = row[3];
-    st.cluster_y_sum = row[4];
-    st.cluster_count = __float_as_int(row[5]);
-    return st;
-}
-
 __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__restrict__ obs,
                                                                 const float *__restrict__ mission,
                                                                 float *__restrict__ prior_out,
@@ -875,7 +817,7 @@ __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__r
                                                                 unsigned int *__restrict__ status) {
     __shared__ RayTables tables;
     extern __shared__ __align__(128) unsigned char dyn[];
-    build_ray_tables(tables);
+    tb_scan::load_tables(tables, threadIdx.x, blockDim.x);
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     WarpSlot &slot = reinterpret_cast<WarpSlot *>(dyn)[warp];
@@ -945,29 +887,17 @@ __global__ void __launch_bounds__(kThreads) onboard_scan_kernel(const float *__r
 
 constexpr int kControlThreads = 128;
 
-__global__ void __launch_bounds__(kControlThreads, 4) onboard_control_kernel(const float *__restrict__ obs,
-                                                                          const float *__restrict__ mission,
-                                                                          float *__restrict__ tactical_out,
-                                                                          float *__restrict__ prior_out,
-                                                                          unsigned long long batch) {
-    const unsigned long long sample = static_cast<unsigned long long>(blockIdx.x) * kControlThreads + threadIdx.x;
-    if (sample >= batch) return;
+/* The control law for one aircraft: the scans' parked results (or the
+ * reference's initial values), then its 24 tactical and 15 prior values into
+ * dst[0..39). */
+__device__ __forceinline__ void control_one(const float *__restrict__ obs, const float *__restrict__ mission,
+                                            const float *__restrict__ parked, unsigned long long sample,
+                                            float *dst) {
     const float *row = obs + sample * kObsDim;
     const float *mrow = mission + sample * kMissionDim;
     bool dodge, slalom;
     scan_modes(mrow, dodge, slalom);
-    RayStats st;
-    if (dodge || slalom) {
-        st = unpark_stats(prior_out + sample * 15);
-    } else {
-        /* the reference's initial values (onboard_features.cuh:188-199) */
-        st.min_r = 30.0f;
-        st.min_r_dx = 0.0f;
-        st.min_r_dy = 0.0f;
-        st.min_dx_c = 30.0f;
-        st.cluster_y_sum = 0.0f;
-        st.cluster_count = 0;
-    }
+    const RayStats st = dodge || slalom ? unpark_stats(parked + sample * 15) : tb_scan::initial_stats();
     float raw_o[48], raw_m[10], o[48], m[10];
     for (int k = 0; k < 48; ++k) {
         raw_o[k] = __ldg(row + k);
@@ -977,8 +907,43 @@ __global__ void __launch_bounds__(kControlThreads, 4) onboard_control_kernel(con
         raw_m[k] = __ldg(mrow + k);
         m[k] = mission_value(raw_m[k]);
     }
-    tactical(raw_o, raw_m, tactical_out + sample * 24);
-    prior(o, m, st, prior_out + sample * 15);
+    tactical(raw_o, raw_m, dst);
+    prior(o, m, st, dst + 24);
+}
+
+constexpr int kOnboardValues = 39; /* 24 tactical + 15 prior; an odd stride: no bank conflicts */
+
+/* One aircraft per thread over a covering grid.  Each thread leaves its 39
+ * values in shared memory; the CTA then writes its rows with coalesced
+ * stores: the tactical and prior rows (contiguous for the CTA's aircraft)
+ * and, with kRows, the onboard columns of the learner's input rows (proprio
+ * columns 52..90, mission columns 10..48; network_gpu.cu:296-302), which the
+ * learner-input kernel leaves to it when it runs the scans itself.  A
+ * scanned aircraft's results are read from its prior row before the CTA's
+ * barrier, and its prior row is overwritten only after it. */
+template <bool kRows>
+__global__ void __launch_bounds__(kControlThreads, 4) onboard_control_kernel(
+    const float *__restrict__ obs, const float *__restrict__ mission, float *__restrict__ tactical_out,
+    float *__restrict__ prior_out, unsigned long long batch, float *__restrict__ proprio,
+    float *__restrict__ mission_vec) {
+    __shared__ float vals[kControlThreads * kOnboardValues];
+    const unsigned long long first = static_cast<unsigned long long>(blockIdx.x) * kControlThreads;
+    const unsigned long long sample = first + threadIdx.x;
+    if (sample < batch) control_one(obs, mission, prior_out, sample, vals + threadIdx.x * kOnboardValues);
+    __syncthreads();
+    const int rows = static_cast<int>(batch - first < kControlThreads ? batch - first : kControlThreads);
+    float *tac = tactical_out + first * 24, *pri = prior_out + first * 15;
+    for (int e = threadIdx.x; e < rows * 24; e += kControlThreads) tac[e] = vals[(e / 24) * kOnboardValues + e % 24];
+    for (int e = threadIdx.x; e < rows * 15; e += kControlThreads)
+        pri[e] = vals[(e / 15) * kOnboardValues + 24 + e % 15];
+    if (kRows) {
+        for (int e = threadIdx.x; e < rows * kOnboardValues; e += kControlThreads) {
+            const unsigned long long r = first + static_cast<unsigned long long>(e / kOnboardValues);
+            const int k = e % kOnboardValues;
+            proprio[r * 91 + 52 + k] = vals[e];
+            mission_vec[r * 49 + 10 + k] = vals[e];
+        }
+    }
 }
 
 constexpr int kMaxDevices = 64;
@@ -986,6 +951,46 @@ constexpr size_t kDynSmem = sizeof(WarpSlot) * kWarps + sizeof(ChunkState); /* a
 int g_sms[kMaxDevices];
 
 } /* namespace */
+
+static int onboard_setup(int *sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+    if (!g_sms[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+        if (cudaFuncSetAttribute(onboard_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kDynSmem)) != cudaSuccess)
+            return 0;
+        g_sms[dev] = n;
+    }
+    *sms = g_sms[dev];
+    return 1;
+}
+
+/* The control-law launch alone (the scans already parked their results in
+ * the prior rows), on `stream`, one aircraft per thread.  With
+ * device_proprio_91 and device_mission_49 both given, it also writes the
+ * onboard columns of those learner rows.  Internal:
+ * tb_cuda_prepare_actor_inputs_device runs it after the learner-input
+ * kernel, which scans the LiDAR rows it has staged. */
+extern "C" int tb_onboard_control_launch(const float *device_obs, const float *device_mission,
+                                         float *device_tactical_24, float *device_prior_15, size_t batch_size,
+                                         void *stream, float *device_proprio_91, float *device_mission_49) {
+    int sms = 0;
+    if (!onboard_setup(&sms)) return 0;
+    if (!device_proprio_91 != !device_mission_49) return 0;
+    cudaGetLastError(); /* report this launch only */
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned int grid = static_cast<unsigned int>((batch_size + kControlThreads - 1) / kControlThreads);
+    if (device_proprio_91)
+        onboard_control_kernel<true><<<grid, kControlThreads, 0, s>>>(
+            device_obs, device_mission, device_tactical_24, device_prior_15, batch_size, device_proprio_91,
+            device_mission_49);
+    else
+        onboard_control_kernel<false><<<grid, kControlThreads, 0, s>>>(
+            device_obs, device_mission, device_tactical_24, device_prior_15, batch_size, nullptr, nullptr);
+    return cudaGetLastError() == cudaSuccess;
+}
 
 /* Both launches; opts may be NULL (its wait_ns and stall_sample fields are
  * honoured: a test withholds one scanning aircraft's staging copy so the
@@ -1001,16 +1006,8 @@ extern "C" int tb_onboard_launch(const float *device_obs, const float *device_mi
         (reinterpret_cast<uintptr_t>(device_tactical_24) & mis) ||
         (reinterpret_cast<uintptr_t>(device_prior_15) & mis))
         return 0;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
-    if (!g_sms[dev]) {
-        int sms = 0;
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-        if (cudaFuncSetAttribute(onboard_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kDynSmem)) != cudaSuccess)
-            return 0;
-        g_sms[dev] = sms;
-    }
+    int sms = 0;
+    if (!onboard_setup(&sms)) return 0;
     const unsigned long long wait_ns = (opts && opts->wait_ns) ? opts->wait_ns : kWaitNs;
     const long long stall_sample = opts ? opts->stall_sample : -1;
     unsigned int *status = tb_status_slot(stream);
@@ -1018,15 +1015,14 @@ extern "C" int tb_onboard_launch(const float *device_obs, const float *device_mi
     cudaGetLastError(); /* report these launches only */
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     /* scans: one CTA per SM (shared memory admits one) */
-    unsigned long long grid = static_cast<unsigned long long>(g_sms[dev]);
+    unsigned long long grid = static_cast<unsigned long long>(sms);
     if (grid > batch_size) grid = batch_size;
     onboard_scan_kernel<<<static_cast<unsigned int>(grid), kThreads, kDynSmem, s>>>(
         device_obs, device_mission, device_prior_15, batch_size, wait_ns, stall_sample, status);
+    if (cudaGetLastError() != cudaSuccess) return 0;
     /* control law: one thread per aircraft */
-    const unsigned long long control_grid = (batch_size + kControlThreads - 1) / kControlThreads;
-    onboard_control_kernel<<<static_cast<unsigned int>(control_grid), kControlThreads, 0, s>>>(
-        device_obs, device_mission, device_tactical_24, device_prior_15, batch_size);
-    return cudaGetLastError() == cudaSuccess;
+    return tb_onboard_control_launch(device_obs, device_mission, device_tactical_24, device_prior_15, batch_size,
+                                     stream, nullptr, nullptr);
 }
 
 extern "C" int tb_cuda_extract_onboard_device(const float *device_obs, const float *device_mission,

@@ -75,13 +75,29 @@ int tb_status_clear(void *stream);
 int tb_onboard_launch(const float *obs, const float *mission, float *tactical, float *prior, size_t batch,
                       void *stream, const tb_features_launch_opts *opts);
 
-/* The learner-input streaming kernel alone (tactical and prior already in
- * place), as tb_cuda_prepare_actor_inputs_device launches it after the
- * onboard kernel; opts may be NULL (wait_ns and stall_sample are honoured). */
+/* The control law alone (the scans' results already parked in the prior
+ * rows), one aircraft per thread on `stream`; with proprio_91 and mission_49
+ * both non-NULL it also writes the tactical and prior values into those
+ * learner rows (proprio columns 52..90, mission columns 10..48). */
+int tb_onboard_control_launch(const float *obs, const float *mission, float *tactical, float *prior, size_t batch,
+                              void *stream, float *proprio_91, float *mission_49);
+
+/* The learner-input streaming kernel alone, tactical and prior already in
+ * place (it copies them into the proprio and mission rows); opts may be NULL
+ * (wait_ns and stall_sample are honoured). */
 int tb_actor_inputs_launch(const float *obs, const float *mission, const unsigned char *cameras,
                            const float *tactical, const float *prior, float *proprio, float *mission_vec,
                            float *lidar, float *luma, size_t batch, void *stream,
                            const tb_features_launch_opts *opts);
+
+/* The learner-input streaming kernel as tb_cuda_prepare_actor_inputs_device
+ * launches it: it also runs the onboard LiDAR scans of the dodge and slalom
+ * aircraft from the rows it has staged, parks their results in the prior
+ * rows, and leaves the onboard columns of the proprio and mission rows to
+ * tb_onboard_control_launch; opts as tb_actor_inputs_launch. */
+int tb_actor_inputs_scan_launch(const float *obs, const float *mission, const unsigned char *cameras,
+                                float *prior, float *proprio, float *mission_vec, float *lidar, float *luma,
+                                size_t batch, void *stream, const tb_features_launch_opts *opts);
 
 /* Launch geometry of the staged kernel on the current device. */
 int tb_features_staged_config(int *blocks_per_sm, int *sms, int *smem_bytes, int *threads,
