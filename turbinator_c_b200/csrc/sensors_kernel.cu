@@ -30,10 +30,14 @@
  *    (|q|^2 within 1e-9 of 1) with finite geometry are culled; anything else
  *    keeps every sphere.  Likewise the arena dome is skipped (unit attitudes
  *    only) for a unit whose origin is so far inside it that every dome hit
- *    lies beyond the sky.
+ *    lies beyond the sky.  Camera units then cull again per warp: each warp
+ *    renders a 16 x 16 pixel tile, tests the unit's list against its tile's
+ *    own cone (the same test) and traces its pixels against the spheres left
+ *    (24-89 spheres in the heaviest scenes, a few per tile).
  *  - Body-frame ray directions do not depend on the scene: they are built on
  *    the host with the C library the simulator uses (sensor_rays.c) and read
- *    from global memory (SoA, coalesced); the kernel only rotates them.
+ *    from global memory (SoA, the camera's in tile order, coalesced); the
+ *    kernel only rotates them.
  *  - The LiDAR noise stream is SplitMix64, whose state after k draws is
  *    seed + k * golden, so ray k hashes its own state without a sequential
  *    pass.
@@ -43,8 +47,9 @@
  *    rounded, so ranges equal the simulator's bit for bit.  The only
  *    transcendental per ray is the camera's exp(-d/80), evaluated once per
  *    unit for sky pixels (whose distance is the unit's constant sky distance).
- *  - Camera bytes are written four pixels per 32-bit store (a warp covers 128
- *    contiguous bytes); the optional raw capture writes each pixel 3 x 3.
+ *  - Camera bytes are written four pixels per 32-bit store (a warp covers
+ *    eight 16-byte row segments of its tile); the optional raw capture
+ *    writes each pixel 3 x 3.
  *  The work is FP64-pipe and issue bound (no tensor-core or HBM bound
  *  applies): about 35 double operations to rotate a ray plus about 8 per
  *  sphere tested.
@@ -88,12 +93,28 @@ static_assert(kThreads >= 32 * kSphereWarps && kUnitRays % (4 * kThreads) == 0, 
 /* Body-frame directions, structure of arrays. */
 __device__ double g_lidar_x[kLidarBins], g_lidar_y[kLidarBins], g_lidar_z[kLidarBins];
 __device__ unsigned int g_lidar_blocked[kLidarBins / 32];
+/* Camera directions in tile order: entry (unit * 8 + warp) * 256 + e is the
+ * camera kernel's entry e of tile `warp` of camera unit `unit` (tile_pixel),
+ * so a warp's loads of its 256 rays are contiguous. */
 __device__ double g_camera_x[kCameraPixels], g_camera_y[kCameraPixels], g_camera_z[kCameraPixels];
 /* The same camera directions rounded to float, for the float pixel test. */
 __device__ float g_camera_fx[kCameraPixels], g_camera_fy[kCameraPixels], g_camera_fz[kCameraPixels];
 /* Per unit kind: body-frame cone axis (unit) and cos, sin of its half-angle
  * widened by 1e-6 rad. */
 __device__ double g_cone[kUnitsPerScene][5];
+/* The same per camera tile: camera unit (view * 2 + half), warp (the warp's
+ * 16 x 16 pixels, rows 16 (w / 4) .. of the half, columns 16 (w % 4) ..). */
+constexpr int kCameraUnits = 8;
+__device__ double g_tile_cone[kCameraUnits][kThreads / 32][5];
+constexpr int kTileCols = 16;                        /* a warp's tile: 256 / kTileCols rows of kTileCols */
+constexpr int kTileRows = 256 / kTileCols;
+constexpr int kTilesAcross = 64 / kTileCols;
+/* first pixel of camera unit `unit`'s tile `warp`, and entry e's pixel */
+__host__ __device__ constexpr int tile_first(int unit, int warp) {
+    return (unit >> 1) * 4096 + (unit & 1) * 2048 + (warp / kTilesAcross) * kTileRows * 64 +
+           (warp % kTilesAcross) * kTileCols;
+}
+__host__ __device__ constexpr int tile_pixel(int first, int e) { return first + (e / kTileCols) * 64 + e % kTileCols; }
 
 struct Vec {
     double x, y, z;
@@ -141,6 +162,13 @@ struct UnitScene {
     int kept_obstacles, kept_opponent, kept_total; /* the unit's list, in trace order */
     unsigned int keep_mask[kSphereWarps], obst_mask[kSphereWarps], opp_mask[kSphereWarps];
     int valid_count, warps_done; /* LiDAR valid rays of the unit, warps finished */
+};
+
+/* A camera tile's sphere list (camera kernel, one per warp). */
+struct TileSpheres {
+    float4 f_oc[kMaxSpheres];         /* UnitScene::f_oc of the listed spheres */
+    float f_margin_ray[kMaxSpheres];  /* UnitScene::f_margin_ray of the listed spheres */
+    unsigned char index[kMaxSpheres]; /* their places in the unit's list, increasing */
 };
 
 /* sphere_hit (sensors.c:4-10) with the ray-independent terms precomputed in
@@ -252,6 +280,65 @@ __device__ __forceinline__ double trace(const UnitScene &s, Vec d, int &kind) {
     return best;
 }
 
+/* One sphere test of trace(): the float miss test, then the double one. */
+__device__ __forceinline__ void tile_sphere(const UnitScene &s, int i, Vec d, float dxf, float dyf, float dzf,
+                                            double &best, int &kind, int k) {
+    if (certain_miss(s, i, dxf, dyf, dzf)) return;
+    const double t = sphere_hit(s, i, d, best);
+    if (t < best) {
+        best = t;
+        kind = k;
+    }
+}
+
+/* trace() for the rays of one camera tile: the same tests in the same order,
+ * over the tile's own sphere list (`index`: n_obst obstacles, then the
+ * opponent when n_opp, then balls, n in all) -- the kept spheres that some
+ * ray of the tile may hit.  The others are proved missed by every ray of the
+ * tile, so skipping them leaves the nearest hit and its kind as they were. */
+__device__ __forceinline__ double trace_tile(const UnitScene &s, Vec d, int &kind, const unsigned char *index,
+                                             int n_obst, int n_opp, int n) {
+    double best = s.h.best0;
+    kind = -1;
+    const double ox = s.h.origin[0], oy = s.h.origin[1], oz = s.h.origin[2];
+    const float dxf = __double2float_rn(d.x), dyf = __double2float_rn(d.y), dzf = __double2float_rn(d.z);
+    if (d.z < -1e-5) {
+        const double t = (0 - oz) / d.z;
+        if (t > 0.05 && t < best) {
+            best = t;
+            kind = 0;
+        }
+        if (s.h.shelf) {
+            const double t2 = (9 - oz) / d.z;
+            if (t2 > 0.05 && t2 < best && ox + t2 * d.x >= 20) {
+                best = t2;
+                kind = 0;
+            }
+        }
+    }
+    int k = 0;
+    for (; k < n_obst; ++k) tile_sphere(s, index[k], d, dxf, dyf, dzf, best, kind, 1);
+    if (s.h.arena) {
+        if (n_opp) {
+            tile_sphere(s, index[k], d, dxf, dyf, dzf, best, kind, 2);
+            ++k;
+        }
+        if (s.h.dome) {
+            const double a = d.x * d.x + d.y * d.y, b = 2 * (ox * d.x + oy * d.y);
+            const double disc = b * b - 4 * a * s.h.dome_cc;
+            if (a > 1e-9 && disc >= 0) {
+                const double td = (-b + sqrt(disc)) / (2 * a);
+                if (td > 0.05 && td < best) {
+                    best = td;
+                    kind = 3;
+                }
+            }
+        }
+    }
+    for (; k < n; ++k) tile_sphere(s, index[k], d, dxf, dyf, dzf, best, kind, 4);
+    return best;
+}
+
 /* shade()'s distance factor, sensors.c:66. */
 __device__ __forceinline__ double fog(double distance) { return 0.75 + 0.25 * exp(-distance / 80); }
 
@@ -294,6 +381,28 @@ __device__ __forceinline__ unsigned long long splitmix(unsigned long long z) {
     z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
     z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
     return z ^ (z >> 31);
+}
+
+/* cone_misses() below for any cone (world-frame unit axis, cos and sin of its
+ * half-angle; the camera tiles use it) -- true when no ray of the cone from
+ * the origin can take a sphere (centre at w from the origin, radius ra) as
+ * its nearest hit: the sphere's surface lies beyond the
+ * sky distance best0 (every hit t >= L - r), or every ray provably returns
+ * "no hit" -- the sphere lies wholly behind the origin, or each ray's closest
+ * approach to the centre exceeds the radius by 1e-6 * max(1, L).  NaN and
+ * infinite inputs give false. */
+__device__ __forceinline__ bool cone_misses_at(double wx, double wy, double wz, double ra, const double *axis,
+                                               double cos_a, double sin_a, double best0) {
+    const double l = sqrt(wx * wx + wy * wy + wz * wz);
+    if (!(l < 1e7) || !(l > ra + 0.1)) return false; /* also rejects NaN */
+    if (l - ra > best0 * (1 + 1e-9) + 1e-9) return true;
+    const double cosc = fmin(1.0, fmax(-1.0, (wx * axis[0] + wy * axis[1] + wz * axis[2]) / l));
+    const double sinc = sqrt(fmax(0.0, 1.0 - cosc * cosc));
+    /* the smallest angle between a ray of the cone and the centre direction */
+    const double sin_min = sinc * cos_a - cosc * sin_a;
+    const double cos_min = cosc * cos_a + sinc * sin_a;
+    if (cos_min < -1e-9 && sin_min > 0) return true; /* every ray points away */
+    return sin_min > 0 && l * sin_min > ra + 1e-6 * fmax(1.0, l);
 }
 
 /* True when no ray of the unit's cone can take the sphere (centre c, radius
@@ -462,7 +571,7 @@ __device__ __forceinline__ void prepare_unit(UnitScene &s, const tb_sensor_scene
  * scene: each view's two halves) run as two kernels, so that each keeps only
  * its own code and registers (one kernel over all ten units spilled more and
  * ran 6-13 % slower with the float tests). */
-constexpr int kLidarUnits = 2, kCameraUnits = 8;
+constexpr int kLidarUnits = 2;
 
 /* LiDAR head `part` of scene `scene_index` (sensors.c:31-49). */
 __device__ __forceinline__ void render_lidar(UnitScene &s, int part, unsigned long long scene_index, float *lidar,
@@ -521,32 +630,63 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
     fu.best0 = s.h.best0;
     fu.best0_lo = __double2float_rn(s.h.best0 * (1 - 1e-6));
     fu.best0_hi = __double2float_rn(s.h.best0 * (1 + 1e-6));
-    const tbf_sphere *fspheres = reinterpret_cast<const tbf_sphere *>(s.f_oc);
     const int view = (part - 2) >> 1, half = (part - 2) & 1;
-    /* Each warp owns 256 pixels of the unit: rows of 128 at 128 w and
-     * 1024 + 128 w, lane l pixels 4l..4l+3 of each.  Pass 1 decides them in
-     * float; the undecided ones go to a per-warp queue, which pass 2 traces
-     * in double one pixel per lane (so a warp pays the double path only for
-     * its undecided pixels, not whenever one lane has one); pass 3 writes the
-     * bytes four to a 32-bit store. */
+    /* Each warp owns a 16 x 16 tile of the unit's 32 x 64 pixels (tile rows
+     * w / 4, columns w % 4); entry e is tile row e / 16, column e % 16, and
+     * lane l takes entries 4l..4l+3 and 128 + 4l..131 + 4l (four pixels of a
+     * row each).  First the warp lists, in trace order, the kept spheres
+     * that some ray of its tile may hit (the unit culling's cone test against
+     * the tile's own cone, g_tile_cone), with their float terms copied beside
+     * the list; then pass 1 decides its pixels in float; the undecided
+     * ones go to a per-warp queue, which pass 2 traces in double one pixel
+     * per lane (so a warp pays the double path only for its undecided pixels,
+     * not whenever one lane has one); pass 3 writes the bytes four to a
+     * 32-bit store. */
     __shared__ __align__(16) unsigned char warp_bytes[kWarps][256];
     __shared__ unsigned char warp_queue[kWarps][256];
+    __shared__ TileSpheres warp_spheres[kWarps];
     const int warp = t >> 5, lane = t & 31;
     unsigned char *bytes = warp_bytes[warp];
     unsigned char *queue = warp_queue[warp];
-    const int first = view * 4096 + half * kUnitRays + warp * 128; /* pixel of the warp's entry 0 */
-    auto pixel_of = [first](int e) { return first + (e >> 7) * 1024 + (e & 127); };
+    TileSpheres &ts = warp_spheres[warp];
+    int n = 0, n_obst = 0, n_opp = 0; /* the tile's list: all, obstacles, opponent (0 or 1) */
+    const int first = tile_first(part - 2, warp); /* pixel of entry 0 */
+    auto pixel_of = [first](int e) { return tile_pixel(first, e); };
+    const int tbase = ((part - 2) * kWarps + warp) * 256; /* the tile's rays in the tile-ordered tables */
+    if (s.kept_total > 0) {
+        const double *cone = g_tile_cone[part - 2][warp];
+        const Vec axis = rotate(qw, qx, qy, qz, Vec{cone[0], cone[1], cone[2]});
+        const double ax[3] = {axis.x, axis.y, axis.z};
+        for (int k = 0; k * 32 < s.kept_total; ++k) {
+            const int i = k * 32 + lane;
+            bool keep = i < s.kept_total;
+            if (keep && s.h.cull) {
+                const double2 xy = s.oc_xy[i], zq = s.oc_zq[i];
+                keep = !cone_misses_at(-xy.x, -xy.y, -zq.x, sqrt(s.rr[i]), ax, cone[3], cone[4], s.h.best0);
+            }
+            const unsigned int m = __ballot_sync(0xffffffffu, keep);
+            if (keep) {
+                const int pos = n + __popc(m & ((1u << lane) - 1u));
+                ts.f_oc[pos] = s.f_oc[i];
+                ts.f_margin_ray[pos] = s.f_margin_ray[i];
+                ts.index[pos] = static_cast<unsigned char>(i);
+            }
+            n += __popc(m);
+            n_obst += __popc(__ballot_sync(0xffffffffu, keep && i < s.kept_obstacles));
+            n_opp += __popc(__ballot_sync(0xffffffffu, keep && s.kept_opponent && i == s.kept_obstacles));
+        }
+        __syncwarp();
+    }
     int queued = 0;
 #pragma unroll 1
     for (int k = 0; k < 2; ++k) {
 #pragma unroll 1
         for (int j = 0; j < 4; ++j) {
             const int e = k * 128 + 4 * lane + j;
-            const int pixel = pixel_of(e);
             unsigned int byte = 0;
-            const bool done = float_unit && tbf_camera_pixel(&fu, fspheres, s.f_margin_ray, s.kept_total,
-                                                             g_camera_fx[pixel], g_camera_fy[pixel],
-                                                             g_camera_fz[pixel], &byte);
+            const bool done = float_unit && tbf_camera_pixel(&fu, reinterpret_cast<const tbf_sphere *>(ts.f_oc),
+                                                             ts.f_margin_ray, n, g_camera_fx[tbase + e],
+                                                             g_camera_fy[tbase + e], g_camera_fz[tbase + e], &byte);
             if (done) bytes[e] = static_cast<unsigned char>(byte);
             const unsigned int pending = __ballot_sync(0xffffffffu, !done);
             if (!done) queue[queued + __popc(pending & ((1u << lane) - 1u))] = static_cast<unsigned char>(e);
@@ -557,10 +697,10 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
 #pragma unroll 1
     for (int q = lane; q < queued; q += 32) {
         const int e = queue[q];
-        const int pixel = pixel_of(e);
-        const Vec dir = rotate(qw, qx, qy, qz, Vec{g_camera_x[pixel], g_camera_y[pixel], g_camera_z[pixel]});
+        const Vec dir =
+            rotate(qw, qx, qy, qz, Vec{g_camera_x[tbase + e], g_camera_y[tbase + e], g_camera_z[tbase + e]});
         int kind;
-        const double d = trace(s, dir, kind);
+        const double d = trace_tile(s, dir, kind, ts.index, n_obst, n_opp, n);
         bytes[e] = static_cast<unsigned char>(shade(s, d, kind, dir.z));
     }
     __syncwarp();
@@ -658,6 +798,20 @@ void unit_cone(const double *x, const double *y, const double *z, int first, int
     cone[4] = sin(widest);
 }
 
+/* Cone of camera tile `warp` of camera unit `unit` (view unit / 2, half
+ * unit % 2): its 16 x 16 pixels, as the camera kernel assigns them. */
+void tile_cone(const double *x, const double *y, const double *z, int unit, int warp, double *cone) {
+    static double tx[256], ty[256], tz[256];
+    const int first = tile_first(unit, warp);
+    for (int e = 0; e < 256; ++e) {
+        const int pixel = tile_pixel(first, e);
+        tx[e] = x[pixel];
+        ty[e] = y[pixel];
+        tz[e] = z[pixel];
+    }
+    unit_cone(tx, ty, tz, 0, 256, nullptr, cone);
+}
+
 /* Uploads the body-frame ray tables and unit cones to the current device (once). */
 bool ensure_tables(int dev) {
     std::lock_guard<std::mutex> lock(g_tables_mutex);
@@ -670,6 +824,7 @@ bool ensure_tables(int dev) {
     static float cfx[kCameraPixels], cfy[kCameraPixels], cfz[kCameraPixels];
     static unsigned int mask[kLidarBins / 32];
     static double cones[kUnitsPerScene][5];
+    static double tile_cones[kCameraUnits][kWarps][5];
     if (!built) {
         tb_sensor_lidar_rays(lidar_dirs, blocked);
         tb_sensor_camera_rays(camera_dirs);
@@ -690,6 +845,26 @@ bool ensure_tables(int dev) {
         for (int h = 0; h < 2; ++h) unit_cone(lx, ly, lz, h * kUnitRays, kUnitRays, blocked, cones[h]);
         for (int p = 2; p < kUnitsPerScene; ++p)
             unit_cone(cx, cy, cz, ((p - 2) >> 1) * 4096 + ((p - 2) & 1) * kUnitRays, kUnitRays, nullptr, cones[p]);
+        for (int u = 0; u < kCameraUnits; ++u)
+            for (int w = 0; w < kWarps; ++w) tile_cone(cx, cy, cz, u, w, tile_cones[u][w]);
+        /* the camera tables in tile order */
+        static double px[kCameraPixels], py[kCameraPixels], pz[kCameraPixels];
+        for (int i = 0; i < kCameraPixels; ++i) {
+            px[i] = cx[i];
+            py[i] = cy[i];
+            pz[i] = cz[i];
+        }
+        for (int u = 0; u < kCameraUnits; ++u)
+            for (int w = 0; w < kWarps; ++w)
+                for (int e = 0; e < 256; ++e) {
+                    const int k = (u * kWarps + w) * 256 + e, pixel = tile_pixel(tile_first(u, w), e);
+                    cx[k] = px[pixel];
+                    cy[k] = py[pixel];
+                    cz[k] = pz[pixel];
+                    cfx[k] = static_cast<float>(px[pixel]);
+                    cfy[k] = static_cast<float>(py[pixel]);
+                    cfz[k] = static_cast<float>(pz[pixel]);
+                }
         built = true;
     }
     int sms = 0, blocks = 0;
@@ -704,6 +879,7 @@ bool ensure_tables(int dev) {
         cudaMemcpyToSymbol(g_camera_fy, cfy, sizeof cfy) != cudaSuccess ||
         cudaMemcpyToSymbol(g_camera_fz, cfz, sizeof cfz) != cudaSuccess ||
         cudaMemcpyToSymbol(g_cone, cones, sizeof cones) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_tile_cone, tile_cones, sizeof tile_cones) != cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, sensors_kernel<false>, kThreads, 0) != cudaSuccess)
         return false;
