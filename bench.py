@@ -637,7 +637,8 @@ def h2d_probe(dev, rank, world, local_rank, barrier):
     in turn (its own PCIe link, nothing else busy), then all ranks at once
     from buffers allocated as the benchmark allocates them, then all ranks at
     once from buffers allocated by a thread bound to the GPU's own NUMA node
-    (the pages land in that node's memory)."""
+    (the pages land in that node's memory).  The same 1 GiB device-to-host,
+    alone and all at once, bounds the gather (which copies the other way)."""
     import torch
 
     nbytes = 1 << 30
@@ -650,6 +651,12 @@ def h2d_probe(dev, rank, world, local_rank, barrier):
         torch.cuda.synchronize(dev)
         return time.perf_counter() - t0
 
+    def back_s():
+        t0 = time.perf_counter()
+        src.copy_(dst, non_blocking=True)
+        torch.cuda.synchronize(dev)
+        return time.perf_counter() - t0
+
     copy_s(src)
     solo = None
     for r in range(world):
@@ -659,6 +666,15 @@ def h2d_probe(dev, rank, world, local_rank, barrier):
         barrier()
     barrier()
     together = copy_s(src)
+    back_s()
+    back_solo = None
+    for r in range(world):
+        barrier()
+        if r == rank:
+            back_solo = back_s()
+        barrier()
+    barrier()
+    back_together = back_s()
     node = gpu_numa_node(local_rank)
     src_local = local = None
     if node is not None and node_cpus(node):
@@ -676,7 +692,9 @@ def h2d_probe(dev, rank, world, local_rank, barrier):
     if src_local is not None:
         local = copy_s(src_local)
     everyone = all_ranks({"solo_gbs": nbytes / solo / 1e9, "together_gbs": nbytes / together / 1e9,
-                          "together_s": together, "numa_local_s": local, "gpu_numa_node": node})
+                          "together_s": together, "numa_local_s": local, "gpu_numa_node": node,
+                          "d2h_solo_gbs": nbytes / back_solo / 1e9, "d2h_together_gbs": nbytes / back_together / 1e9,
+                          "d2h_together_s": back_together})
     del src, dst, src_local
     torch.cuda.empty_cache()
     if hasattr(torch._C, "_host_emptyCache"):
@@ -686,8 +704,12 @@ def h2d_probe(dev, rank, world, local_rank, barrier):
            "together_gbs": [e["together_gbs"] for e in everyone],
            "together_aggregate_gbs": world * nbytes / max(e["together_s"] for e in everyone) / 1e9,
            "gpu_numa_node": [e["gpu_numa_node"] for e in everyone],
-           "method": "torch copy_ of a 1 GiB page-locked buffer to the device, host wall clock; solo: one "
-                     "rank at a time; together: all ranks at once, aggregate = N GiB / slowest rank"}
+           "d2h_solo_gbs": [e["d2h_solo_gbs"] for e in everyone],
+           "d2h_together_gbs": [e["d2h_together_gbs"] for e in everyone],
+           "d2h_together_aggregate_gbs": world * nbytes / max(e["d2h_together_s"] for e in everyone) / 1e9,
+           "method": "torch copy_ of a 1 GiB page-locked buffer to the device (and back: d2h_*), host wall "
+                     "clock; solo: one rank at a time; together: all ranks at once, aggregate = N GiB / "
+                     "slowest rank"}
     if all(e["numa_local_s"] for e in everyone):
         out["numa_local_aggregate_gbs"] = world * nbytes / max(e["numa_local_s"] for e in everyone) / 1e9
         out["numa_local_gbs"] = [nbytes / e["numa_local_s"] / 1e9 for e in everyone]
@@ -1054,10 +1076,24 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         gatherer.gather(d_out, stream)
         stream.synchronize()
         c3_times.append(time.perf_counter() - t0)
+    # the same slices copied into each rank's own page-locked buffer (which no
+    # other rank can read): what the shared mapping itself costs
+    private = torch.empty((count, tb.FEATURE_DIM), dtype=torch.float32, pin_memory=True)
+    p_times = []
+    for _ in range(reps):
+        barrier()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            private.copy_(d_out, non_blocking=True)
+        stream.synchronize()
+        p_times.append(time.perf_counter() - t0)
+    del private
     barrier()
     if tb.tb_cuda_synchronize(stream.cuda_stream) != 1:
         raise RuntimeError("feature kernel reported a pipeline timeout (gather leg)")
     g_max = statistics.median(max_over_ranks_list(g_times))
+    p_max = statistics.median(max_over_ranks_list(p_times))
     c3_max = statistics.median(max_over_ranks_list(c3_times))
     gather_bytes = total * tb.FEATURE_DIM * 4
     gather = {"ms": g_max * 1e3, "bytes_to_host": gather_bytes, "gbs": gather_bytes / g_max / 1e9,
@@ -1066,7 +1102,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                     "host buffer shared by all ranks (/dev/shm, cudaHostRegister per rank), concurrently; "
                     "no GPU collective",
               "timing": f"host wall clock from a barrier to the copy's completion, max over ranks per "
-                        f"repetition, median of {reps}"}
+                        f"repetition, median of {reps}",
+              "private_buffers_ms": p_max * 1e3,
+              "private_buffers_note": "the same copies into each rank's own page-locked torch buffer at once"}
     config3_e2e = {"value": total / c3_max, "unit": UNIT, "ms": c3_max * 1e3,
                    "op": "one feature launch on resident inputs plus the gather of its output to host memory",
                    "timing": f"host wall clock from a barrier, max over ranks per repetition, median of {reps}"}
