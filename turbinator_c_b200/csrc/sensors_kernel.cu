@@ -107,6 +107,7 @@ __device__ double g_cone[kUnitsPerScene][5];
 constexpr int kCameraUnits = 8;
 __device__ double g_tile_cone[kCameraUnits][kThreads / 32][5];
 constexpr int kTileCols = 16;                        /* a warp's tile: 256 / kTileCols rows of kTileCols */
+static_assert((kThreads / 32) * 256 == 2048, "one 256-pixel tile per warp covers a camera unit's 2,048 pixels");
 constexpr int kTileRows = 256 / kTileCols;
 constexpr int kTilesAcross = 64 / kTileCols;
 /* first pixel of camera unit `unit`'s tile `warp`, and entry e's pixel */
