@@ -170,6 +170,7 @@ struct TileSpheres {
     float4 f_oc[kMaxSpheres];         /* UnitScene::f_oc of the listed spheres */
     float f_margin_ray[kMaxSpheres];  /* UnitScene::f_margin_ray of the listed spheres */
     unsigned char index[kMaxSpheres]; /* their places in the unit's list, increasing */
+    int n_obst, n_opp;                /* listed obstacles, opponent (0 or 1) */
 };
 
 /* sphere_hit (sensors.c:4-10) with the ray-independent terms precomputed in
@@ -676,8 +677,12 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
             n_obst += __popc(__ballot_sync(0xffffffffu, keep && i < s.kept_obstacles));
             n_opp += __popc(__ballot_sync(0xffffffffu, keep && s.kept_opponent && i == s.kept_obstacles));
         }
-        __syncwarp();
     }
+    if (lane == 0) { /* read back by pass 2 only */
+        ts.n_obst = n_obst;
+        ts.n_opp = n_opp;
+    }
+    __syncwarp();
     int queued = 0;
 #pragma unroll 1
     for (int k = 0; k < 2; ++k) {
@@ -701,7 +706,7 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
         const Vec dir =
             rotate(qw, qx, qy, qz, Vec{g_camera_x[tbase + e], g_camera_y[tbase + e], g_camera_z[tbase + e]});
         int kind;
-        const double d = trace_tile(s, dir, kind, ts.index, n_obst, n_opp, n);
+        const double d = trace_tile(s, dir, kind, ts.index, ts.n_obst, ts.n_opp, n);
         bytes[e] = static_cast<unsigned char>(shade(s, d, kind, dir.z));
     }
     __syncwarp();
