@@ -10,9 +10,10 @@
  *   tb_rand64 (SplitMix64), physics.c:73-78.
  *
  * Design (B200):
- *  - Work unit = 2,048 rays of one scene: LiDAR head 0 or 1, or one half
- *    (32 rows) of one camera view -- 10 units per scene, one CTA per unit,
- *    CTAs striding over units.  Each unit traces from a single origin, so the
+ *  - Work unit = the rays of one scene from one origin: LiDAR head 0 or 1
+ *    (2,048 rays) or one camera view (4,096 rays, rendered as two halves of
+ *    32 rows) -- 6 units per scene, one CTA per unit, CTAs striding over
+ *    units.  Each unit traces from a single origin, so the
  *    ray-independent sphere terms (o - c, |o - c|^2, r^2) and the dome's
  *    constant term are formed once per CTA in shared memory and read as warp
  *    broadcasts (two 128-bit and one 64-bit load per sphere).  Two
@@ -80,7 +81,7 @@ namespace {
 constexpr int kThreads = TB_SENSOR_THREADS;
 constexpr int kWarps = kThreads / 32;
 constexpr int kUnitRays = 2048;
-constexpr int kUnitsPerScene = 10; /* 2 LiDAR heads + 4 views x 2 halves */
+constexpr int kUnitsPerScene = 6; /* 2 LiDAR heads + 4 camera views */
 constexpr int kMaxSpheres = TB_SENSOR_MAX_OBSTACLES + 1 + TB_SENSOR_MAX_BALLS;
 constexpr int kSphereWarps = (kMaxSpheres + 31) / 32;
 constexpr int kLidarBins = TB_SENSOR_LIDAR_BINS;
@@ -93,24 +94,24 @@ static_assert(kThreads >= 32 * kSphereWarps && kUnitRays % (4 * kThreads) == 0, 
 /* Body-frame directions, structure of arrays. */
 __device__ double g_lidar_x[kLidarBins], g_lidar_y[kLidarBins], g_lidar_z[kLidarBins];
 __device__ unsigned int g_lidar_blocked[kLidarBins / 32];
-/* Camera directions in tile order: entry (unit * 8 + warp) * 256 + e is the
- * camera kernel's entry e of tile `warp` of camera unit `unit` (tile_pixel),
- * so a warp's loads of its 256 rays are contiguous. */
+/* Camera directions in tile order: entry (half * 8 + warp) * 256 + e is the
+ * camera kernel's entry e of tile `warp` of view half `half` (view * 2 + top
+ * or bottom; tile_pixel), so a warp's loads of its 256 rays are contiguous. */
 __device__ double g_camera_x[kCameraPixels], g_camera_y[kCameraPixels], g_camera_z[kCameraPixels];
 /* The same camera directions rounded to float, for the float pixel test. */
 __device__ float g_camera_fx[kCameraPixels], g_camera_fy[kCameraPixels], g_camera_fz[kCameraPixels];
 /* Per unit kind: body-frame cone axis (unit) and cos, sin of its half-angle
  * widened by 1e-6 rad. */
 __device__ double g_cone[kUnitsPerScene][5];
-/* The same per camera tile: camera unit (view * 2 + half), warp (the warp's
+/* The same per camera tile: view half (view * 2 + half), warp (the warp's
  * 16 x 16 pixels, rows 16 (w / 4) .. of the half, columns 16 (w % 4) ..). */
-constexpr int kCameraUnits = 8;
-__device__ double g_tile_cone[kCameraUnits][kThreads / 32][5];
+constexpr int kCameraHalves = 8; /* camera view halves (32 rows each) per scene: view * 2 + half */
+__device__ double g_tile_cone[kCameraHalves][kThreads / 32][5];
 constexpr int kTileCols = 16;                        /* a warp's tile: 256 / kTileCols rows of kTileCols */
 static_assert((kThreads / 32) * 256 == 2048, "one 256-pixel tile per warp covers a camera unit's 2,048 pixels");
 constexpr int kTileRows = 256 / kTileCols;
 constexpr int kTilesAcross = 64 / kTileCols;
-/* first pixel of camera unit `unit`'s tile `warp`, and entry e's pixel */
+/* first pixel of view half `unit`'s (view * 2 + half) tile `warp`, and entry e's pixel */
 __host__ __device__ constexpr int tile_first(int unit, int warp) {
     return (unit >> 1) * 4096 + (unit & 1) * 2048 + (warp / kTilesAcross) * kTileRows * 64 +
            (warp % kTilesAcross) * kTileCols;
@@ -446,7 +447,7 @@ __device__ __forceinline__ void unit_head(UnitHead &h, const tb_sensor_scene *__
     if (part < 2) {
         mount = Vec{0.4, 0.4, part ? -0.4 : 0.4};
     } else {
-        const int view = (part - 2) >> 1;
+        const int view = part - 2;
         mount = view < 2 ? Vec{0.42, 0.42, view == 0 ? 0.13 : 0.08} : Vec{0, 0, view == 2 ? -0.5 : 0.5};
     }
     const Vec r = rotate(qw, qx, qy, qz, mount);
@@ -573,7 +574,7 @@ __device__ __forceinline__ void prepare_unit(UnitScene &s, const tb_sensor_scene
  * scene: each view's two halves) run as two kernels, so that each keeps only
  * its own code and registers (one kernel over all ten units spilled more and
  * ran 6-13 % slower with the float tests). */
-constexpr int kLidarUnits = 2;
+constexpr int kLidarUnits = 2, kCameraUnits = 4;
 
 /* LiDAR head `part` of scene `scene_index` (sensors.c:31-49). */
 __device__ __forceinline__ void render_lidar(UnitScene &s, int part, unsigned long long scene_index, float *lidar,
@@ -616,7 +617,8 @@ __device__ __forceinline__ void render_lidar(UnitScene &s, int part, unsigned lo
     }
 }
 
-/* Half of camera view (part - 2) / 2 of scene `scene_index` (sensors.c:71-79): 32 rows of 64. */
+/* Camera view part - 2 of scene `scene_index` (sensors.c:71-79): 64 rows of 64, rendered as
+ * two halves of 32 rows (one 16 x 16 tile of each per warp) after a single setup of the unit. */
 __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned long long scene_index,
                                               unsigned char *cameras, unsigned char *raw) {
     const int t = threadIdx.x;
@@ -632,7 +634,7 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
     fu.best0 = s.h.best0;
     fu.best0_lo = __double2float_rn(s.h.best0 * (1 - 1e-6));
     fu.best0_hi = __double2float_rn(s.h.best0 * (1 + 1e-6));
-    const int view = (part - 2) >> 1, half = (part - 2) & 1;
+    const int view = part - 2;
     /* Each warp owns a 16 x 16 tile of the unit's 32 x 64 pixels (tile rows
      * w / 4, columns w % 4); entry e is tile row e / 16, column e % 16, and
      * lane l takes entries 4l..4l+3 and 128 + 4l..131 + 4l (four pixels of a
@@ -651,12 +653,15 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
     unsigned char *bytes = warp_bytes[warp];
     unsigned char *queue = warp_queue[warp];
     TileSpheres &ts = warp_spheres[warp];
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+    const int hu = view * 2 + half; /* the view half: index of the tile tables */
     int n = 0, n_obst = 0, n_opp = 0; /* the tile's list: all, obstacles, opponent (0 or 1) */
-    const int first = tile_first(part - 2, warp); /* pixel of entry 0 */
+    const int first = tile_first(hu, warp); /* pixel of entry 0 */
     auto pixel_of = [first](int e) { return tile_pixel(first, e); };
-    const int tbase = ((part - 2) * kWarps + warp) * 256; /* the tile's rays in the tile-ordered tables */
+    const int tbase = (hu * kWarps + warp) * 256; /* the tile's rays in the tile-ordered tables */
     if (s.kept_total > 0) {
-        const double *cone = g_tile_cone[part - 2][warp];
+        const double *cone = g_tile_cone[hu][warp];
         const Vec axis = rotate(qw, qx, qy, qz, Vec{cone[0], cone[1], cone[2]});
         const double ax[3] = {axis.x, axis.y, axis.z};
         for (int k = 0; k * 32 < s.kept_total; ++k) {
@@ -737,7 +742,8 @@ __device__ __forceinline__ void render_camera(UnitScene &s, int part, unsigned l
             }
         }
     }
-    __syncwarp(); /* the buffers are refilled by the next unit */
+    __syncwarp(); /* the buffers are refilled by the next half or unit */
+    }
 }
 
 template <bool kLidar>
@@ -804,7 +810,7 @@ void unit_cone(const double *x, const double *y, const double *z, int first, int
     cone[4] = sin(widest);
 }
 
-/* Cone of camera tile `warp` of camera unit `unit` (view unit / 2, half
+/* Cone of camera tile `warp` of view half `unit` (view unit / 2, half
  * unit % 2): its 16 x 16 pixels, as the camera kernel assigns them. */
 void tile_cone(const double *x, const double *y, const double *z, int unit, int warp, double *cone) {
     static double tx[256], ty[256], tz[256];
@@ -830,7 +836,7 @@ bool ensure_tables(int dev) {
     static float cfx[kCameraPixels], cfy[kCameraPixels], cfz[kCameraPixels];
     static unsigned int mask[kLidarBins / 32];
     static double cones[kUnitsPerScene][5];
-    static double tile_cones[kCameraUnits][kWarps][5];
+    static double tile_cones[kCameraHalves][kWarps][5];
     if (!built) {
         tb_sensor_lidar_rays(lidar_dirs, blocked);
         tb_sensor_camera_rays(camera_dirs);
@@ -849,9 +855,8 @@ bool ensure_tables(int dev) {
             cfz[i] = static_cast<float>(cz[i]);
         }
         for (int h = 0; h < 2; ++h) unit_cone(lx, ly, lz, h * kUnitRays, kUnitRays, blocked, cones[h]);
-        for (int p = 2; p < kUnitsPerScene; ++p)
-            unit_cone(cx, cy, cz, ((p - 2) >> 1) * 4096 + ((p - 2) & 1) * kUnitRays, kUnitRays, nullptr, cones[p]);
-        for (int u = 0; u < kCameraUnits; ++u)
+        for (int p = 2; p < kUnitsPerScene; ++p) unit_cone(cx, cy, cz, (p - 2) * 4096, 4096, nullptr, cones[p]);
+        for (int u = 0; u < kCameraHalves; ++u)
             for (int w = 0; w < kWarps; ++w) tile_cone(cx, cy, cz, u, w, tile_cones[u][w]);
         /* the camera tables in tile order */
         static double px[kCameraPixels], py[kCameraPixels], pz[kCameraPixels];
@@ -860,7 +865,7 @@ bool ensure_tables(int dev) {
             py[i] = cy[i];
             pz[i] = cz[i];
         }
-        for (int u = 0; u < kCameraUnits; ++u)
+        for (int u = 0; u < kCameraHalves; ++u)
             for (int w = 0; w < kWarps; ++w)
                 for (int e = 0; e < 256; ++e) {
                     const int k = (u * kWarps + w) * 256 + e, pixel = tile_pixel(tile_first(u, w), e);
