@@ -102,13 +102,18 @@ def test_float_ground_test_never_contradicts_the_double_division():
 
 
 def float_rotate(q, v):
-    """tb_camera_float.h's rotation: tb_rotate's formula, every operation in float."""
+    """tb_camera_float.h's rotation: tb_rotate's formula in float, each
+    multiply-add fused (one rounding) as the header writes it."""
     qw, qx, qy, qz = (q[:, i:i + 1].astype(F32) for i in range(4))
     vx, vy, vz = (v[None, :, i].astype(F32) for i in range(3))
-    cx, cy, cz = qy * vz - qz * vy, qz * vx - qx * vz, qx * vy - qy * vx
+
+    def fma(a, b, c):
+        return (np.asarray(a, np.float64) * np.asarray(b, np.float64) + np.asarray(c, np.float64)).astype(F32)
+
+    cx, cy, cz = fma(qy, vz, -(qz * vy)), fma(qz, vx, -(qx * vz)), fma(qx, vy, -(qy * vx))
     tx, ty, tz = cx * F32(2), cy * F32(2), cz * F32(2)
-    ax, ay, az = vx + tx * qw, vy + ty * qw, vz + tz * qw
-    return ax + (qy * tz - qz * ty), ay + (qz * tx - qx * tz), az + (qx * ty - qy * tx)
+    ax, ay, az = fma(tx, qw, vx), fma(ty, qw, vy), fma(tz, qw, vz)
+    return ax + fma(qy, tz, -(qz * ty)), ay + fma(qz, tx, -(qx * tz)), az + fma(qx, ty, -(qy * tx))
 
 
 def double_rotate(q, v):

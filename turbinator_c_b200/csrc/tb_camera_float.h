@@ -14,11 +14,14 @@
  * dome test was written, checked bit for bit and dropped: it decided more
  * pixels but cost more time than it saved.)
  *
- * Error bounds, u = 2^-24, all arithmetic plain float (the kernel's file is
- * built without contraction):
+ * Error bounds, u = 2^-24, in float arithmetic where each multiply-add is
+ * written as one fused operation (TBF_FMA, rounded once; the kernel's file
+ * is otherwise built without contraction).  A fused a * b + c rounds once
+ * where the separate product and sum round twice, so every bound below,
+ * derived for separate roundings, holds for it too:
  *  - Direction: tb_rotate's formula with |q| = 1 (to 1e-9) and |v| = 1, in
  *    float from float copies of q and v, is within 35 u = 2.1e-6 of the
- *    double direction per component (each of the 18 operations rounds by u
+ *    double direction per component (each of at most 18 roundings is by u
  *    of a value <= 2, and the inputs by u).  TBF_ED = 8e-6 is used.
  *  - Sphere miss: b = oc.d in float is within sqrt(3) L TBF_ED + 5 u L of
  *    the double b (L = |oc|); b*b + (r^2 - L^2) is then within
@@ -46,10 +49,12 @@
 #ifdef __CUDACC__
 #define TBF_FN static __device__ __forceinline__
 #define TBF_EXPF(x) __expf(x)
+#define TBF_FMA(a, b, c) __fmaf_rn((a), (b), (c))
 #define TBF_FDIV(a, b) __fdividef((a), (b)) /* within 2 ulp for |b| in [2^-126, 2^126] */
 #else
 #define TBF_FN static inline
 #define TBF_EXPF(x) expf(x)
+#define TBF_FMA(a, b, c) fmaf((a), (b), (c)) /* correctly rounded, like the GPU's */
 #define TBF_FDIV(a, b) ((a) / (b))
 #endif
 
@@ -75,13 +80,14 @@ typedef struct tbf_sphere {
 TBF_FN int tbf_camera_pixel(const tbf_unit *u, const tbf_sphere *spheres, const float *margins, int n, float vx,
                             float vy, float vz, unsigned int *byte) {
     const float qw = u->qw, qx = u->qx, qy = u->qy, qz = u->qz;
-    const float cx = qy * vz - qz * vy, cy = qz * vx - qx * vz, cz = qx * vy - qy * vx;
+    const float cx = TBF_FMA(qy, vz, -(qz * vy)), cy = TBF_FMA(qz, vx, -(qx * vz)), cz = TBF_FMA(qx, vy, -(qy * vx));
     const float tx = cx * 2.0f, ty = cy * 2.0f, tz = cz * 2.0f;
-    const float ax = vx + tx * qw, ay = vy + ty * qw, az = vz + tz * qw;
-    const float dx = ax + (qy * tz - qz * ty), dy = ay + (qz * tx - qx * tz), dz = az + (qx * ty - qy * tx);
+    const float ax = TBF_FMA(tx, qw, vx), ay = TBF_FMA(ty, qw, vy), az = TBF_FMA(tz, qw, vz);
+    const float dx = ax + TBF_FMA(qy, tz, -(qz * ty)), dy = ay + TBF_FMA(qz, tx, -(qx * tz)),
+                dz = az + TBF_FMA(qx, ty, -(qy * tx));
     for (int i = 0; i < n; ++i) {
-        const float b = spheres[i].x * dx + spheres[i].y * dy + spheres[i].z * dz;
-        if (!(b * b + spheres[i].w < -margins[i])) return 0;
+        const float b = TBF_FMA(spheres[i].z, dz, TBF_FMA(spheres[i].y, dy, spheres[i].x * dx));
+        if (!(TBF_FMA(b, b, spheres[i].w) < -margins[i])) return 0;
     }
     int ground = 0;
     float t = 0.0f, rel = 0.0f;
@@ -103,12 +109,12 @@ TBF_FN int tbf_camera_pixel(const tbf_unit *u, const tbf_sphere *spheres, const 
     }
     float x, m;
     if (ground) {
-        const float luma = 0.28f + 0.17f * fminf(1.0f, fmaxf(0.0f, -dz));
+        const float luma = TBF_FMA(0.17f, fminf(1.0f, fmaxf(0.0f, -dz)), 0.28f);
         const float e = TBF_EXPF(t * -0.0125f);
-        x = luma * (0.75f + 0.25f * e) * 255.0f;
+        x = luma * TBF_FMA(0.25f, e, 0.75f) * 255.0f;
         m = 255.0f * (0.17f * TBF_ED + 0.00625f * (e + 1e-6f) * t * rel + 6e-7f);
     } else {
-        x = (0.22f + 0.15f * fminf(1.0f, fmaxf(-1.0f, dz))) * u->sky_fog * 255.0f;
+        x = TBF_FMA(0.15f, fminf(1.0f, fmaxf(-1.0f, dz)), 0.22f) * u->sky_fog * 255.0f;
         m = 255.0f * (0.15f * TBF_ED + 5e-7f);
     }
     m += 8e-6f;
