@@ -1,6 +1,9 @@
-"""The sensor kernel's float decisions (turbinator_c_b200/csrc/sensors_kernel.cu:
-certain_miss and the camera ground test in trace) restated with numpy float32
-arithmetic and checked against the double arithmetic they stand in for, on
+"""The sensor kernel's float shortcuts restated with numpy float32 arithmetic
+(certain_miss in turbinator_c_b200/csrc/sensors_kernel.cu; a float ground test
+with relatively widened limits, the form the float camera decision in
+tb_camera_float.h builds on -- that header's own bounds are checked bit for bit
+by tests/test_sensors_oracle.py; and the float direction's error) and checked
+against the double arithmetic they stand in for, on
 cases built to sit at the decision boundaries: rays tangent to a sphere within
 a relative 1e-12 .. 1e-3, spheres from 1 mm to 1e6 m away, and ground rays
 grazing the 0.05 m and sky-distance limits.  A float decision may decline to
