@@ -10,15 +10,16 @@
  *   tb_rand64 (SplitMix64), physics.c:73-78.
  *
  * Design (B200):
- *  - Work unit = the rays of one scene from one origin: LiDAR head 0 or 1
- *    (2,048 rays) or one camera view (4,096 rays, rendered as two halves of
- *    32 rows) -- 6 units per scene, one CTA per unit, CTAs striding over
+ *  - Work unit = a scene's two LiDAR heads (2 x 2,048 rays from two origins,
+ *    both sphere lists formed in one setup, the heads rendered in turn) or
+ *    one camera view (4,096 rays from one origin, rendered as two halves of
+ *    32 rows) -- 5 units per scene, one CTA per unit, CTAs striding over
  *    units.  Each unit traces from a single origin, so the
  *    ray-independent sphere terms (o - c, |o - c|^2, r^2) and the dome's
  *    constant term are formed once per CTA in shared memory and read as warp
  *    broadcasts (two 128-bit and one 64-bit load per sphere).  Two
- *    shared-memory slots alternate over a CTA's units, so a unit costs two CTA
- *    barriers (both while its sphere list is formed); the LiDAR valid count is
+ *    shared-memory slots (pairs for LiDAR) alternate over a CTA's units, so a
+ *    unit costs two CTA barriers (both while its sphere lists are formed); the LiDAR valid count is
  *    summed with shared-memory atomics and written by the last warp.
  *  - Sphere culling per unit: a sphere whose surface lies farther than the
  *    sky distance can never beat it, and a unit's rays lie in a cone (axis
@@ -485,11 +486,17 @@ __device__ __forceinline__ void unit_head(UnitHead &h, const tb_sensor_scene *__
              static_cast<unsigned long long>(static_cast<long long>(scene->player) * 257);
 }
 
-/* Forms unit `part` of `scene` in s: the first warps form the scalars and the
- * sphere list (two CTA barriers in all); every thread returns after the
- * second, with s complete. */
-__device__ __forceinline__ void prepare_unit(UnitScene &s, const tb_sensor_scene *__restrict__ scene, int part) {
-    const int t = threadIdx.x;
+/* Forms unit `part0` of `scene` in s0 and, with `two`, unit part0 + 1 in s1:
+ * the first kSphereWarps warps form a unit's scalars and sphere list, the
+ * next kSphereWarps warps the second unit's, in the same two CTA barriers;
+ * every thread returns after the second, with the units complete. */
+__device__ __forceinline__ void prepare_units(UnitScene &s0, UnitScene &s1, const tb_sensor_scene *__restrict__ scene,
+                                              int part0, bool two) {
+    static_assert(2 * 32 * kSphereWarps <= kThreads, "two units' sphere warps");
+    const bool second = two && threadIdx.x >= 32 * kSphereWarps; /* warp-uniform */
+    UnitScene &s = second ? s1 : s0;
+    const int part = part0 + (second ? 1 : 0);
+    const int t = static_cast<int>(threadIdx.x) - (second ? 32 * kSphereWarps : 0);
     double ocx = 0, ocy = 0, ocz = 0, occ = 0, rr = 0;
     bool keep = false, float_test = false;
     int n_obst = 0, arena = 0;
@@ -754,22 +761,29 @@ __global__ void __launch_bounds__(kThreads, TB_SENSOR_MIN_BLOCKS)
     /* Two slots, alternating over the units this CTA renders: a slot is
      * rewritten only after both barriers of the unit in between, which every
      * thread passes after it finished tracing from that slot. */
-    __shared__ UnitScene slots[2];
-    constexpr int kPerScene = kLidar ? kLidarUnits : kCameraUnits;
+    __shared__ UnitScene slots[kLidar ? 4 : 2];
+    /* LiDAR: one unit per scene, both heads formed in one setup (their own
+     * origins, so two sphere lists) and rendered in turn */
+    constexpr int kPerScene = kLidar ? 1 : kCameraUnits;
     int used = 0;
     for (unsigned long long unit = blockIdx.x; unit < units; unit += gridDim.x) {
         const unsigned long long scene_index = unit / kPerScene;
-        const int part = static_cast<int>(unit - scene_index * kPerScene) + (kLidar ? 0 : kLidarUnits);
+        const int part = kLidar ? 0 : static_cast<int>(unit - scene_index * kPerScene) + kLidarUnits;
         const tb_sensor_scene *scene = scenes + scene_index;
         /* the same word for every thread: a CTA-uniform skip */
         if (!(scene->sensors & (kLidar ? TB_SENSOR_LIDAR : TB_SENSOR_CAMERA))) continue;
-        UnitScene &s = slots[used & 1];
-        ++used;
-        prepare_unit(s, scene, part);
-        if constexpr (kLidar)
-            render_lidar(s, part, scene_index, lidar, lidar_stride, lidar_valid, valid_stride);
-        else
+        if constexpr (kLidar) {
+            UnitScene &s0 = slots[(used & 1) * 2], &s1 = slots[(used & 1) * 2 + 1];
+            ++used;
+            prepare_units(s0, s1, scene, 0, true);
+            render_lidar(s0, 0, scene_index, lidar, lidar_stride, lidar_valid, valid_stride);
+            render_lidar(s1, 1, scene_index, lidar, lidar_stride, lidar_valid, valid_stride);
+        } else {
+            UnitScene &s = slots[used & 1];
+            ++used;
+            prepare_units(s, s, scene, part, false);
             render_camera(s, part, scene_index, cameras, raw);
+        }
     }
 }
 
@@ -921,7 +935,7 @@ extern "C" int tb_cuda_render_sensors_device(const tb_sensor_scene *device_scene
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned long long cap = static_cast<unsigned long long>(g_grid_cap[dev]);
     if (device_lidar) {
-        const unsigned long long units = static_cast<unsigned long long>(count) * kLidarUnits;
+        const unsigned long long units = static_cast<unsigned long long>(count); /* both heads per unit */
         sensors_kernel<true><<<static_cast<unsigned int>(units < cap ? units : cap), kThreads, 0, s>>>(
             device_scenes, units, device_lidar, lidar_stride, device_lidar_valid, valid_stride, nullptr, nullptr);
     }
